@@ -1,0 +1,115 @@
+"""ctypes binding of the C ABI (include/fp8linear_b200.h).
+
+This is the binding a non-torch host would write against ``libfp8linear_b200.so``;
+here it takes torch CUDA tensors only as carriers of device pointers and streams.
+Every call checks the returned status and raises ``RuntimeError`` with the
+library's message on failure.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libfp8linear_b200.so"
+
+OK = 0
+DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+DTYPE_NONE = -1
+
+# name -> (restype, argtypes); mirrors the declarations in include/fp8linear_b200.h
+_P, _I, _I64, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+SIGNATURES = {
+    "fp8lin_abi_version": (_I, []),
+    "fp8lin_build_info": (ctypes.c_char_p, []),
+    "fp8lin_last_error": (ctypes.c_char_p, []),
+    "fp8lin_quantize_fp8": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
+    "fp8lin_quantize_weight": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
+    "fp8lin_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
+    "fp8lin_linear_workspace_size": (_SZ, [_I64, _I64]),
+    "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+    "fp8lin_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
+}
+
+
+class CApi:
+    def __init__(self, path: str | Path = LIB_PATH):
+        self.path = Path(path)
+        if not self.path.exists():
+            raise ImportError(f"{self.path} not built; run `python -m fp8linear_b200._build`")
+        self.lib = ctypes.CDLL(str(self.path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(self.lib, name)
+            fn.restype = res
+            fn.argtypes = args
+
+    # -- helpers
+    def _check(self, rc: int, op: str) -> None:
+        if rc != OK:
+            raise RuntimeError(f"{op} failed (status {rc}): {self.last_error()}")
+
+    def last_error(self) -> str:
+        return self.lib.fp8lin_last_error().decode()
+
+    @staticmethod
+    def _stream(t: torch.Tensor | None = None) -> int:
+        dev = t.device if t is not None else torch.device("cuda")
+        return torch.cuda.current_stream(dev).cuda_stream
+
+    # -- entry points
+    def quantize_fp8(self, x: torch.Tensor, xq: torch.Tensor | None = None,
+                     scale: torch.Tensor | None = None):
+        M, K = x.shape
+        xq = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device) if xq is None else xq
+        scale = torch.empty((M,), dtype=torch.float32, device=x.device) if scale is None else scale
+        rc = self.lib.fp8lin_quantize_fp8(x.data_ptr(), DTYPE[x.dtype], M, K, xq.data_ptr(),
+                                          scale.data_ptr(), self._stream(x))
+        self._check(rc, "fp8lin_quantize_fp8")
+        return xq, scale
+
+    def quantize_weight(self, w: torch.Tensor):
+        N, K = w.shape
+        wq = torch.empty((N, K), dtype=torch.float8_e4m3fn, device=w.device)
+        scale = torch.empty((N,), dtype=torch.float32, device=w.device)
+        rc = self.lib.fp8lin_quantize_weight(w.data_ptr(), DTYPE[w.dtype], N, K, wq.data_ptr(),
+                                             scale.data_ptr(), self._stream(w))
+        self._check(rc, "fp8lin_quantize_weight")
+        return wq, scale
+
+    def fp8_gemm(self, xq, x_scale, wq, w_scale, bias=None, out_dtype=torch.bfloat16, out=None):
+        M, K = xq.shape
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=out_dtype, device=xq.device) if out is None else out
+        rc = self.lib.fp8lin_fp8_gemm(
+            xq.data_ptr(), x_scale.data_ptr(), wq.data_ptr(), w_scale.data_ptr(),
+            None if bias is None else bias.data_ptr(),
+            DTYPE_NONE if bias is None else DTYPE[bias.dtype],
+            out.data_ptr(), DTYPE[out.dtype], M, N, K, self._stream(xq))
+        self._check(rc, "fp8lin_fp8_gemm")
+        return out
+
+    def workspace_size(self, M: int, K: int) -> int:
+        return int(self.lib.fp8lin_linear_workspace_size(M, K))
+
+    def fp8_linear(self, x, wq, w_scale, bias=None, out=None, workspace=None):
+        M, K = x.shape
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device) if out is None else out
+        need = self.workspace_size(M, K)
+        if workspace is None:
+            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=x.device)
+        rc = self.lib.fp8lin_fp8_linear(
+            x.data_ptr(), DTYPE[x.dtype], wq.data_ptr(), w_scale.data_ptr(),
+            None if bias is None else bias.data_ptr(),
+            DTYPE_NONE if bias is None else DTYPE[bias.dtype],
+            out.data_ptr(), DTYPE[out.dtype], M, N, K, workspace.data_ptr(),
+            workspace.numel(), self._stream(x))
+        self._check(rc, "fp8lin_fp8_linear")
+        return out
+
+    def device_status(self, clear: bool = False) -> int:
+        v = ctypes.c_uint(0)
+        self._check(self.lib.fp8lin_device_status(ctypes.byref(v), int(clear)),
+                    "fp8lin_device_status")
+        return int(v.value)

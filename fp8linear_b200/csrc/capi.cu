@@ -1,0 +1,199 @@
+// capi.cu -- the extern "C" boundary (include/fp8linear_b200.h): argument checks that
+// mirror the reference's TORCH_CHECKs, workspace carving for the fused op, and the
+// thread-local error message. No allocation happens here.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/fp8linear_b200.h"
+#include "internal.h"
+
+namespace fp8lin {
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &msg) {
+  set_error(msg);
+  return code;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr size_t kWsAlign = 256;
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+void clear_error() { g_last_error.clear(); }
+
+bool current_device_info(DeviceInfo *info) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    return false;
+  }
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal out of range");
+    return false;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev].device != dev) {
+    DeviceInfo d;
+    d.device = dev;
+    if ((e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev)) !=
+            cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) !=
+            cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) !=
+            cudaSuccess) {
+      set_error(std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+      return false;
+    }
+    cache[dev] = d;
+  }
+  *info = cache[dev];
+  return true;
+}
+
+namespace {
+
+int check_gemm_args(const void *xq, const float *xs, const void *wq, const float *ws,
+                    const void *bias, int bias_dtype, const void *out, int out_dtype, int64_t M,
+                    int64_t N, int64_t K, const char *op) {
+  const std::string o(op);
+  if (M < 0 || N < 0 || K < 0) return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": negative size");
+  if (out_dtype != kBF16 && out_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": out_dtype must be BF16 or F16");
+  if (bias != nullptr && bias_dtype != kBF16 && bias_dtype != kF16 && bias_dtype != kF32)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": bias_dtype must be BF16, F16 or F32");
+  if (K % 16 != 0 || K == 0)
+    return fail(FP8LIN_ERR_UNSUPPORTED,
+                o + ": K must be a positive multiple of 16 for FP8 matmul, got " +
+                    std::to_string(K));
+  if (N % 8 != 0)
+    return fail(FP8LIN_ERR_UNSUPPORTED,
+                o + ": N must be a multiple of 8 (16-byte output rows), got " + std::to_string(N));
+  if (M == 0 || N == 0) return FP8LIN_OK;
+  if (!xq || !xs || !wq || !ws || !out)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": null pointer");
+  if (!aligned(xq, 16) || !aligned(wq, 16) || !aligned(out, 16))
+    return fail(FP8LIN_ERR_UNSUPPORTED, o + ": xq, wq and out must be 16-byte aligned");
+  return FP8LIN_OK;
+}
+
+}  // namespace
+}  // namespace fp8lin
+
+using namespace fp8lin;
+
+extern "C" {
+
+int fp8lin_abi_version(void) { return FP8LIN_ABI_VERSION; }
+
+#define FP8LIN_STR2(x) #x
+#define FP8LIN_STR(x) FP8LIN_STR2(x)
+const char *fp8lin_build_info(void) {
+  return "fp8linear_b200: sm_100a tcgen05 e4m3 GEMM (128x256x128 tiles, 4-stage TMA ring, "
+         "fused dequant+bias epilogue), per-token quantizer; nvcc " FP8LIN_STR(
+             __CUDACC_VER_MAJOR__) "." FP8LIN_STR(__CUDACC_VER_MINOR__);
+}
+
+const char *fp8lin_last_error(void) { return g_last_error.c_str(); }
+
+int fp8lin_quantize_fp8(const void *x, int x_dtype, int64_t M, int64_t K, void *xq,
+                        float *x_scale, void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_fp8: x must be fp16 or bf16");
+  if (M < 0 || K < 0) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_fp8: negative size");
+  if (M == 0) return FP8LIN_OK;
+  if (K == 0) return fail(FP8LIN_ERR_UNSUPPORTED, "quantize_fp8: K must be positive");
+  if (!x || !xq || !x_scale) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_fp8: null pointer");
+  cudaError_t e = launch_quantize_rows(x, x_dtype, M, K, static_cast<uint8_t *>(xq), x_scale,
+                                       static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("quantize_fp8: launch: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
+int fp8lin_quantize_weight(const void *w, int w_dtype, int64_t N, int64_t K, void *wq,
+                           float *w_scale, void *stream) {
+  clear_error();
+  if (w_dtype != kBF16 && w_dtype != kF16 && w_dtype != kF32)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_weight: weight must be bf16, fp16 or fp32");
+  if (N < 0 || K < 0) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_weight: negative size");
+  if (N == 0) return FP8LIN_OK;
+  if (!w || !wq || !w_scale)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_weight: null pointer");
+  cudaError_t e = launch_quantize_weight(w, w_dtype, N, K, static_cast<uint8_t *>(wq), w_scale,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("quantize_weight: launch: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
+int fp8lin_fp8_gemm(const void *xq, const float *x_scale, const void *wq, const float *w_scale,
+                    const void *bias, int bias_dtype, void *out, int out_dtype, int64_t M,
+                    int64_t N, int64_t K, void *stream) {
+  clear_error();
+  int rc = check_gemm_args(xq, x_scale, wq, w_scale, bias, bias_dtype, out, out_dtype, M, N, K,
+                           "fp8_gemm");
+  if (rc != FP8LIN_OK || M == 0 || N == 0) return rc;
+  GemmArgs a{static_cast<const uint8_t *>(xq), x_scale, static_cast<const uint8_t *>(wq),
+             w_scale, bias, bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  return launch_gemm(a, static_cast<cudaStream_t>(stream), false);
+}
+
+size_t fp8lin_linear_workspace_size(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  return round_up(static_cast<size_t>(M) * static_cast<size_t>(K), kWsAlign) +
+         round_up(static_cast<size_t>(M) * sizeof(float), kWsAlign);
+}
+
+int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq, const float *w_scale,
+                      const void *bias, int bias_dtype, void *out, int out_dtype, int64_t M,
+                      int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                      void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear: x must be fp16 or bf16");
+  int rc = check_gemm_args(reinterpret_cast<const void *>(16), w_scale, wq, w_scale, bias,
+                           bias_dtype, out, out_dtype, M, N, K, "fp8_linear");
+  if (rc != FP8LIN_OK || M == 0 || N == 0) return rc;
+  if (!x) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear: null x");
+  const size_t need = fp8lin_linear_workspace_size(M, K);
+  if (!workspace || workspace_bytes < need)
+    return fail(FP8LIN_ERR_WORKSPACE, "fp8_linear: workspace of " + std::to_string(need) +
+                                          " bytes required, got " +
+                                          std::to_string(workspace_bytes));
+  if (!aligned(workspace, kWsAlign))
+    return fail(FP8LIN_ERR_WORKSPACE, "fp8_linear: workspace must be 256-byte aligned");
+  uint8_t *xq = static_cast<uint8_t *>(workspace);
+  float *xs = reinterpret_cast<float *>(
+      xq + round_up(static_cast<size_t>(M) * static_cast<size_t>(K), kWsAlign));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_quantize_rows(x, x_dtype, M, K, xq, xs, s, true);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("fp8_linear: quantize launch: ") +
+                                     cudaGetErrorString(e));
+  GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
+             bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  return launch_gemm(a, s, true);
+}
+
+int fp8lin_device_status(unsigned int *status, int clear) {
+  clear_error();
+  if (!status) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "device_status: null pointer");
+  cudaError_t e = read_gemm_status(status, clear != 0);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("device_status: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
+}  // extern "C"

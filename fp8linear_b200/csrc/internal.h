@@ -1,0 +1,58 @@
+// internal.h -- declarations shared by the kernels' translation units and the C ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include <cuda_runtime.h>
+
+namespace fp8lin {
+
+enum DType : int { kBF16 = 0, kF16 = 1, kF32 = 2, kNone = -1 };
+
+constexpr float kE4M3Max = 448.0f;
+constexpr float kScaleFloor = 1e-12f;
+
+// Thread-local last-error message used by the C ABI.
+void set_error(const std::string &msg);
+void clear_error();
+
+// Per-device facts the launchers need (cached after the first query).
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+};
+// Fills `info` for the calling thread's current device; false + error message on failure.
+bool current_device_info(DeviceInfo *info);
+
+// ---- quantize.cu
+// Per-token quantization (activation path). Returns cudaSuccess or the launch error.
+cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                                 float *scale, cudaStream_t stream, bool trigger_dependents);
+// Per-channel weight quantization (ATen semantics of the reference's quantize_weight).
+cudaError_t launch_quantize_weight(const void *w, int dtype, int64_t N, int64_t K, uint8_t *wq,
+                                   float *scale, cudaStream_t stream);
+
+// ---- gemm_sm100.cu
+struct GemmArgs {
+  const uint8_t *xq;
+  const float *xs;
+  const uint8_t *wq;
+  const float *ws;
+  const void *bias;
+  int bias_dtype;
+  void *out;
+  int out_dtype;
+  int64_t M, N, K;
+};
+// Launches the tcgen05 GEMM + fused epilogue. `pdl` launches it as a programmatic
+// dependent of the previous kernel on the stream. Returns an fp8lin_status code and
+// sets the error message on failure.
+int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl);
+// Reads (and optionally clears) the GEMM watchdog bits of the current device.
+cudaError_t read_gemm_status(unsigned int *bits, bool clear);
+
+}  // namespace fp8lin

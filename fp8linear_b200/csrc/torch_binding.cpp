@@ -1,0 +1,233 @@
+// torch_binding.cpp -- TORCH_LIBRARY registration of the reference's op surface on
+// top of the C ABI in libfp8linear_b200.so.
+//
+// Same schemas as the reference (torch-ext/torch_binding.cpp:7-27), registered for
+// the CUDA dispatch key only, under the namespace `fp8linear_b200`. Host code here
+// only checks arguments (the reference's TORCH_CHECKs, csrc/quantize.cu:200-204 and
+// csrc/fp8_gemm.cu:144-160), allocates outputs with the caching allocator and calls
+// the C ABI on the current stream of the tensors' device. There is no CPU path and
+// no fallback: a failing kernel call raises.
+//
+// Output dtype: the reference's fp8_gemm/fp8_linear always return fp16
+// (csrc/fp8_gemm.cu:163). Here fp8_linear returns x's dtype (bf16 for bf16 input,
+// fp16 for fp16 input) and fp8_gemm returns bf16.
+//
+// The reference's MXFP8 / NVFP4 schemas (torch-ext/torch_binding.cpp:30-65) are
+// registered so that code probing for them finds them, and raise a clear error.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+#include <torch/torch.h>
+
+#include "../../include/fp8linear_b200.h"
+
+namespace {
+
+int dtype_code(at::ScalarType t) {
+  switch (t) {
+    case at::kBFloat16: return FP8LIN_DTYPE_BF16;
+    case at::kHalf: return FP8LIN_DTYPE_F16;
+    case at::kFloat: return FP8LIN_DTYPE_F32;
+    default: return -2;
+  }
+}
+
+void check_rc(int rc, const char *op) {
+  TORCH_CHECK(rc == FP8LIN_OK, op, " failed (status ", rc, "): ", fp8lin_last_error());
+}
+
+void *stream_of(const at::Tensor &t) {
+  return static_cast<void *>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+// A fresh allocation is 16-byte aligned; a view with an odd storage offset may not be.
+at::Tensor aligned16(const at::Tensor &t) {
+  auto c = t.contiguous();
+  if (reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 != 0) c = c.clone();
+  return c;
+}
+
+std::tuple<at::Tensor, at::Tensor> quantize_fp8(at::Tensor x) {
+  TORCH_CHECK(x.is_cuda(), "x must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
+              "x must be fp16 or bf16");
+  TORCH_CHECK(x.dim() == 2, "x must be 2D [M, K]");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto xc = x.contiguous();
+  const int64_t M = xc.size(0), K = xc.size(1);
+  auto xq = at::empty_like(xc, xc.options().dtype(at::kFloat8_e4m3fn));
+  auto scale = at::empty({M}, xc.options().dtype(at::kFloat));
+  if (M == 0 || K == 0) {
+    if (M > 0) scale.fill_(1e-12f);  // an empty row has amax 0 -> the scale floor
+    return {xq, scale};
+  }
+  check_rc(fp8lin_quantize_fp8(xc.data_ptr(), dtype_code(xc.scalar_type()), M, K, xq.data_ptr(),
+                               scale.data_ptr<float>(), stream_of(xc)),
+           "quantize_fp8");
+  return {xq, scale};
+}
+
+std::tuple<at::Tensor, at::Tensor> quantize_weight(at::Tensor weight) {
+  TORCH_CHECK(weight.is_cuda() && weight.dim() == 2, "weight must be a 2D CUDA tensor");
+  const int code = dtype_code(weight.scalar_type());
+  TORCH_CHECK(code >= 0, "weight must be bf16, fp16 or fp32");
+  c10::cuda::CUDAGuard guard(weight.device());
+  auto w = weight.detach().contiguous();
+  const int64_t N = w.size(0), K = w.size(1);
+  auto wq = at::empty({N, K}, w.options().dtype(at::kFloat8_e4m3fn));
+  auto scale = at::empty({N}, w.options().dtype(at::kFloat));
+  if (N == 0) return {wq, scale};
+  if (K == 0) {
+    scale.fill_(1e-12f);
+    return {wq, scale};
+  }
+  check_rc(fp8lin_quantize_weight(w.data_ptr(), code, N, K, wq.data_ptr(),
+                                  scale.data_ptr<float>(), stream_of(w)),
+           "quantize_weight");
+  return {wq, scale};
+}
+
+struct BiasArg {
+  at::Tensor t;
+  const void *ptr = nullptr;
+  int dtype = FP8LIN_DTYPE_NONE;
+};
+
+BiasArg prep_bias(const std::optional<at::Tensor> &bias, int64_t N) {
+  BiasArg b;
+  if (!bias.has_value() || !bias->defined()) return b;
+  TORCH_CHECK(bias->is_cuda(), "bias must be on CUDA");
+  TORCH_CHECK(bias->numel() == N, "bias must have N entries");
+  b.t = bias->contiguous();
+  if (dtype_code(b.t.scalar_type()) < 0) b.t = b.t.to(at::kFloat);
+  b.ptr = b.t.data_ptr();
+  b.dtype = dtype_code(b.t.scalar_type());
+  return b;
+}
+
+at::Tensor gemm_impl(const at::Tensor &xq, const at::Tensor &x_scale, const at::Tensor &wq,
+                     const at::Tensor &w_scale, const std::optional<at::Tensor> &bias,
+                     at::ScalarType out_dtype) {
+  TORCH_CHECK(xq.is_cuda() && wq.is_cuda(), "inputs must be on CUDA");
+  TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn,
+              "xq and wq must be float8_e4m3fn");
+  TORCH_CHECK(xq.dim() == 2 && wq.dim() == 2, "xq, wq must be 2D");
+  TORCH_CHECK(xq.size(1) == wq.size(1), "K mismatch: xq[M,K], wq[N,K]");
+  c10::cuda::CUDAGuard guard(xq.device());
+  auto xqc = aligned16(xq);
+  auto wqc = aligned16(wq);
+  const int64_t M = xqc.size(0), K = xqc.size(1), N = wqc.size(0);
+  TORCH_CHECK(K % 16 == 0, "K must be a multiple of 16 for FP8 matmul, got ", K);
+  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8 (16-byte bf16 output rows), got ", N);
+  auto xs = x_scale.contiguous();
+  auto ws = w_scale.contiguous();
+  TORCH_CHECK(xs.scalar_type() == at::kFloat && ws.scalar_type() == at::kFloat,
+              "scales must be fp32");
+  TORCH_CHECK(xs.numel() == M, "x_scale must have M entries (per-token)");
+  TORCH_CHECK(ws.numel() == N, "w_scale must have N entries (per-channel)");
+  TORCH_CHECK(xs.is_cuda() && ws.is_cuda(), "scales must be on CUDA");
+  auto out = at::empty({M, N}, xqc.options().dtype(out_dtype));
+  if (M == 0 || N == 0) return out;
+  TORCH_CHECK(K > 0, "K must be positive");
+  BiasArg b = prep_bias(bias, N);
+  check_rc(fp8lin_fp8_gemm(xqc.data_ptr(), xs.data_ptr<float>(), wqc.data_ptr(),
+                           ws.data_ptr<float>(), b.ptr, b.dtype, out.data_ptr(),
+                           dtype_code(out_dtype), M, N, K, stream_of(xqc)),
+           "fp8_gemm");
+  return out;
+}
+
+at::Tensor fp8_gemm(at::Tensor xq, at::Tensor x_scale, at::Tensor wq, at::Tensor w_scale,
+                    std::optional<at::Tensor> bias) {
+  return gemm_impl(xq, x_scale, wq, w_scale, bias, at::kBFloat16);
+}
+
+at::Tensor fp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scale,
+                      std::optional<at::Tensor> bias) {
+  TORCH_CHECK(x.is_cuda() && wq.is_cuda(), "inputs must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
+              "x must be fp16 or bf16");
+  TORCH_CHECK(x.dim() >= 1, "x must have at least one dimension");
+  if (w_scale.scalar_type() == at::kByte)
+    TORCH_CHECK(false,
+                "fp8_linear: uint8 (MXFP8/NVFP4 block) weight scales are not supported by "
+                "fp8linear_b200; quantize the weight with quantize_weight (per-channel fp32 "
+                "scales)");
+  TORCH_CHECK(wq.scalar_type() == at::kFloat8_e4m3fn, "wq must be float8_e4m3fn");
+  TORCH_CHECK(wq.dim() == 2, "wq must be 2D [N, K]");
+  TORCH_CHECK(w_scale.scalar_type() == at::kFloat, "w_scale must be fp32");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(wq.size(1) == K, "K mismatch: x[..., K], wq[N, K]");
+  auto x2d = aligned16(x.reshape({-1, K}));
+  auto wqc = aligned16(wq);
+  const int64_t M = x2d.size(0), N = wqc.size(0);
+  TORCH_CHECK(K % 16 == 0, "K must be a multiple of 16 for FP8 matmul, got ", K);
+  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8 (16-byte output rows), got ", N);
+  auto ws = w_scale.contiguous();
+  TORCH_CHECK(ws.numel() == N, "w_scale must have N entries (per-channel)");
+  auto out_shape = x.sizes().vec();
+  out_shape.back() = N;
+  auto out = at::empty({M, N}, x2d.options());
+  if (M > 0 && N > 0) {
+    TORCH_CHECK(K > 0, "K must be positive");
+    BiasArg b = prep_bias(bias, N);
+    const size_t ws_bytes = fp8lin_linear_workspace_size(M, K);
+    auto workspace = at::empty({static_cast<int64_t>(ws_bytes)}, x2d.options().dtype(at::kByte));
+    check_rc(fp8lin_fp8_linear(x2d.data_ptr(), dtype_code(x2d.scalar_type()), wqc.data_ptr(),
+                               ws.data_ptr<float>(), b.ptr, b.dtype, out.data_ptr(),
+                               dtype_code(x2d.scalar_type()), M, N, K, workspace.data_ptr(),
+                               ws_bytes, stream_of(x2d)),
+             "fp8_linear");
+  }
+  return out.reshape(out_shape);
+}
+
+[[noreturn]] void unsupported(const char *name) {
+  TORCH_CHECK(false, name,
+              " is not provided by fp8linear_b200: only the per-channel FP8 path "
+              "(quantize_fp8 / quantize_weight / fp8_gemm / fp8_linear) is implemented");
+}
+
+std::tuple<at::Tensor, at::Tensor> quantize_mxfp8(at::Tensor) { unsupported("quantize_mxfp8"); }
+at::Tensor mxfp8_gemm(at::Tensor, at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
+  unsupported("mxfp8_gemm");
+}
+at::Tensor mxfp8_linear(at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
+  unsupported("mxfp8_linear");
+}
+std::tuple<at::Tensor, at::Tensor> quantize_nvfp4(at::Tensor) { unsupported("quantize_nvfp4"); }
+at::Tensor nvfp4_gemm(at::Tensor, at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
+  unsupported("nvfp4_gemm");
+}
+at::Tensor nvfp4_linear(at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
+  unsupported("nvfp4_linear");
+}
+
+}  // namespace
+
+TORCH_LIBRARY(fp8linear_b200, m) {
+  m.def("quantize_fp8(Tensor x) -> (Tensor, Tensor)");
+  m.def("quantize_weight(Tensor weight) -> (Tensor, Tensor)");
+  m.def("fp8_gemm(Tensor xq, Tensor x_scale, Tensor wq, Tensor w_scale, Tensor? bias) -> Tensor");
+  m.def("fp8_linear(Tensor x, Tensor wq, Tensor w_scale, Tensor? bias) -> Tensor");
+  m.def("quantize_mxfp8(Tensor x) -> (Tensor, Tensor)");
+  m.def("mxfp8_gemm(Tensor xq, Tensor x_scales, Tensor wq, Tensor w_scales, Tensor? bias) -> Tensor");
+  m.def("mxfp8_linear(Tensor x, Tensor wq, Tensor w_scales, Tensor? bias) -> Tensor");
+  m.def("quantize_nvfp4(Tensor x) -> (Tensor, Tensor)");
+  m.def("nvfp4_gemm(Tensor xq, Tensor x_scales, Tensor wq, Tensor w_scales, Tensor? bias) -> Tensor");
+  m.def("nvfp4_linear(Tensor x, Tensor wq, Tensor w_scales, Tensor? bias) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(fp8linear_b200, CUDA, m) {
+  m.impl("quantize_fp8", &quantize_fp8);
+  m.impl("quantize_weight", &quantize_weight);
+  m.impl("fp8_gemm", &fp8_gemm);
+  m.impl("fp8_linear", &fp8_linear);
+  m.impl("quantize_mxfp8", &quantize_mxfp8);
+  m.impl("mxfp8_gemm", &mxfp8_gemm);
+  m.impl("mxfp8_linear", &mxfp8_linear);
+  m.impl("quantize_nvfp4", &quantize_nvfp4);
+  m.impl("nvfp4_gemm", &nvfp4_gemm);
+  m.impl("nvfp4_linear", &nvfp4_linear);
+}

@@ -1,0 +1,140 @@
+"""Python layer API, mirroring torch-ext/fp8linear/layers.py of the reference.
+
+Same public names and contracts:
+  * fake (meta) implementations so ``torch.compile`` traces through the ops
+    (layers.py:11-66 of the reference);
+  * ``quantize_weight`` / ``fp8_linear`` wrappers (layers.py:107-118);
+  * ``quantize_(module)``: in-place e4m3 weight quantization of every eligible
+    ``nn.Linear`` (layers.py:120-142);
+  * ``Fp8Linear``: the stateless kernels-hub layer whose ``forward`` is grafted onto
+    a quantized ``nn.Linear`` (layers.py:145-167).
+
+Differences from the reference: ``fp8_linear`` returns ``x.dtype`` (the reference
+returns fp16 and ``Fp8Linear.forward`` casts back); ``fp8_gemm`` returns bf16; the
+MXFP8 / NVFP4 entry points exist but raise ``NotImplementedError``.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from ._ops import add_op_namespace_prefix, ops
+
+E4M3_MAX = 448.0
+
+
+@torch.library.register_fake(add_op_namespace_prefix("fp8_linear"))
+def _fp8_linear_fake(x, wq, w_scale, bias=None):
+    return x.new_empty((*x.shape[:-1], wq.shape[0]), dtype=x.dtype)
+
+
+@torch.library.register_fake(add_op_namespace_prefix("quantize_fp8"))
+def _quantize_fp8_fake(x):
+    xq = x.new_empty(x.shape, dtype=torch.float8_e4m3fn)
+    scale = x.new_empty((x.shape[0],), dtype=torch.float32)
+    return xq, scale
+
+
+@torch.library.register_fake(add_op_namespace_prefix("quantize_weight"))
+def _quantize_weight_fake(weight):
+    wq = weight.new_empty(weight.shape, dtype=torch.float8_e4m3fn)
+    scale = weight.new_empty((weight.shape[0],), dtype=torch.float32)
+    return wq, scale
+
+
+@torch.library.register_fake(add_op_namespace_prefix("fp8_gemm"))
+def _fp8_gemm_fake(xq, x_scale, wq, w_scale, bias=None):
+    return xq.new_empty((xq.shape[0], wq.shape[0]), dtype=torch.bfloat16)
+
+
+def _not_provided(name: str):
+    raise NotImplementedError(
+        f"{name}: fp8linear_b200 implements the per-channel FP8 path only "
+        "(quantize_fp8 / quantize_weight / fp8_gemm / fp8_linear)"
+    )
+
+
+def quantize_weight_mxfp8(weight: torch.Tensor):
+    """Not provided (the reference's opt-in MXFP8 format); raises NotImplementedError."""
+    _not_provided("quantize_weight_mxfp8")
+
+
+def mxfp8_linear(x, wq, w_scales, bias=None):
+    """Not provided (the reference's opt-in MXFP8 format); raises NotImplementedError."""
+    _not_provided("mxfp8_linear")
+
+
+def quantize_weight_nvfp4(weight: torch.Tensor):
+    """Not provided (the reference's opt-in NVFP4 format); raises NotImplementedError."""
+    _not_provided("quantize_weight_nvfp4")
+
+
+def nvfp4_linear(x, wq, w_scales, bias=None):
+    """Not provided (the reference's opt-in NVFP4 format); raises NotImplementedError."""
+    _not_provided("nvfp4_linear")
+
+
+def quantize_weight(weight: torch.Tensor):
+    """Per-output-channel e4m3 quantization of a ``[N, K]`` CUDA weight (offline).
+
+    Returns ``(wq e4m3 [N, K], w_scale fp32 [N])`` with the reference's arithmetic
+    (csrc/quantize.cu:359-365): ``w_scale = max(amax / 448, 1e-12)`` and
+    ``wq = e4m3(clamp(w / w_scale, -448, 448))``.
+    """
+    return ops.quantize_weight(weight)
+
+
+def fp8_linear(x, wq, w_scale, bias=None):
+    """FP8 linear for pre-quantized weights (``wq``/``w_scale`` from quantize_weight).
+
+    ``x [..., K]`` bf16/fp16 -> ``[..., N]`` in ``x.dtype``: per-token e4m3
+    quantization of x, tcgen05 FP8 GEMM, per-token x per-channel dequant and bias
+    fused in the GEMM epilogue.
+    """
+    return ops.fp8_linear(x, wq, w_scale, bias)
+
+
+@torch.no_grad()
+def quantize_(module: nn.Module) -> int:
+    """In place: quantize every eligible ``nn.Linear`` weight in ``module`` to e4m3.
+
+    The quantized weight replaces ``linear.weight`` (as a buffer) and the per-channel
+    scale is stored as ``linear.weight_scale`` -- the reference's contract
+    (layers.py:120-142), eligibility ``in_features % 16 == 0``. Run it once before
+    grafting ``Fp8Linear.forward`` so weights are never re-quantized per forward.
+    Returns the number of layers converted.
+    """
+    n = 0
+    for child in module.modules():
+        if (
+            isinstance(child, nn.Linear)
+            and child.in_features % 16 == 0
+            and getattr(child, "weight", None) is not None
+            and child.weight.dtype != torch.float8_e4m3fn
+        ):
+            wq, scale = quantize_weight(child.weight.data)
+            del child._parameters["weight"]
+            child.register_buffer("weight", wq)
+            child.register_buffer("weight_scale", scale)
+            n += 1
+    return n
+
+
+class Fp8Linear(nn.Module):
+    """Stateless kernel layer: an ``nn.Linear`` forward on FP8 tensor cores.
+
+    No constructor and no state of its own (the kernels-hub layer contract). The
+    forward is grafted onto a module already converted by ``quantize_``; it reads
+    the host module's e4m3 ``weight``, fp32 ``weight_scale`` and ``bias``.
+    """
+
+    weight: torch.Tensor  # e4m3 [N, K]
+    weight_scale: torch.Tensor  # fp32 [N]
+    bias: torch.Tensor | None
+
+    has_backward: bool = False
+    can_torch_compile: bool = True
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        out = ops.fp8_linear(x, self.weight, self.weight_scale, self.bias)
+        return out.to(x.dtype)

@@ -1,0 +1,139 @@
+/*
+ * fp8linear_b200.h -- C ABI of the B200 (sm_100a) fused FP8 linear.
+ *
+ * Plain pointers and sizes only; no framework types cross this boundary. Every
+ * device pointer is a CUDA device address on the calling thread's current device,
+ * and every call is asynchronous on `stream` (a cudaStream_t passed as void*;
+ * NULL means the legacy default stream). No call synchronises the host or
+ * allocates device memory.
+ *
+ * Each entry point replaces one operator of drbh/fp8linear (paths relative to the
+ * reference project root); the argument meaning and error conditions follow the
+ * reference's host code, with the differences stated per function.
+ *
+ * Return value: FP8LIN_OK (0) or an fp8lin_status error; fp8lin_last_error()
+ * gives this thread's message for the last failed call.
+ */
+#ifndef FP8LINEAR_B200_H
+#define FP8LINEAR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FP8LIN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FP8LIN_API __attribute__((visibility("default")))
+#else
+#define FP8LIN_API
+#endif
+
+typedef enum fp8lin_status {
+  FP8LIN_OK = 0,
+  FP8LIN_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad dtype code */
+  FP8LIN_ERR_UNSUPPORTED = 2,      /* shape/alignment outside what the kernels take */
+  FP8LIN_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  FP8LIN_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
+  FP8LIN_ERR_DEVICE = 5            /* no sm_100 device current */
+} fp8lin_status;
+
+/* Element types (codes shared by every dtype argument). */
+typedef enum fp8lin_dtype {
+  FP8LIN_DTYPE_BF16 = 0,
+  FP8LIN_DTYPE_F16 = 1,
+  FP8LIN_DTYPE_F32 = 2,
+  FP8LIN_DTYPE_NONE = -1 /* "no tensor" (only valid for the optional bias) */
+} fp8lin_dtype;
+
+/* Library ABI version (FP8LIN_ABI_VERSION) and a human-readable build string. */
+FP8LIN_API int fp8lin_abi_version(void);
+FP8LIN_API const char *fp8lin_build_info(void);
+
+/* Message for the last failed call on this thread ("" if none). */
+FP8LIN_API const char *fp8lin_last_error(void);
+
+/*
+ * Per-token dynamic e4m3 quantization.
+ * Replaces quantize_fp8 (csrc/quantize.cu:199-234; kernel csrc/quantize.cu:45-73).
+ *   x       [M, K] row-major, x_dtype BF16 or F16
+ *   xq      [M, K] row-major e4m3fn codes (1 byte each)
+ *   x_scale [M] fp32, x_scale[m] = max(amax_m / 448, 1e-12)
+ * xq[m,k] = e4m3_satfinite(clamp(x[m,k] * (1 / x_scale[m]), -448, 448)), bit-identical
+ * to the reference kernel. M == 0 is a no-op. Any K >= 1 is accepted.
+ */
+FP8LIN_API int fp8lin_quantize_fp8(const void *x, int x_dtype, int64_t M, int64_t K,
+                                   void *xq, float *x_scale, void *stream);
+
+/*
+ * Per-output-channel e4m3 weight quantization (offline, once per weight).
+ * Replaces the per-channel branch of quantize_weight (csrc/quantize.cu:341-366),
+ * which the reference evaluates with ATen ops on the GPU:
+ *   w_scale[n] = max(amax_n * (1/448), 1e-12)   (ATen's scalar divide is a
+ *                                                reciprocal multiply on CUDA)
+ *   wq[n,k]    = e4m3(clamp(w[n,k] / w_scale[n], -448, 448))  (true divide)
+ *   w       [N, K] row-major, w_dtype BF16, F16 or F32
+ *   wq      [N, K] e4m3fn codes; w_scale [N] fp32. NaN propagates as in ATen.
+ * The reference's opt-in MXFP8/NVFP4 diversions (FP8LINEAR_USE_MX /
+ * FP8LINEAR_USE_NVFP4, csrc/quantize.cu:344-357) are not part of this library.
+ */
+FP8LIN_API int fp8lin_quantize_weight(const void *w, int w_dtype, int64_t N, int64_t K,
+                                      void *wq, float *w_scale, void *stream);
+
+/*
+ * FP8 GEMM with the dequant + bias epilogue fused in.
+ * Replaces fp8_gemm (csrc/fp8_gemm.cu:139-194): the cuBLASLt e4m3 matmul into an
+ * fp32 [M,N] buffer (csrc/fp8_gemm.cu:180-184) followed by dequant_bias_kernel
+ * (csrc/fp8_gemm.cu:65-80), here one tcgen05 kernel with no fp32 intermediate:
+ *   out[m,n] = (sum_k xq[m,k]*wq[n,k]) * x_scale[m] * w_scale[n] + bias[n]
+ *   xq [M,K] e4m3 row-major; wq [N,K] e4m3 row-major (K-major, i.e. nn.Linear layout)
+ *   x_scale [M] fp32; w_scale [N] fp32
+ *   bias [N] of bias_dtype (BF16/F16/F32) or NULL with FP8LIN_DTYPE_NONE
+ *   out [M,N] row-major, out_dtype BF16 or F16 (the reference always writes fp16)
+ * Requirements (checked): K % 16 == 0 and K > 0 (as csrc/fp8_gemm.cu:154), N % 8 == 0,
+ * xq/wq/out 16-byte aligned. M == 0 or N == 0 is a no-op.
+ */
+FP8LIN_API int fp8lin_fp8_gemm(const void *xq, const float *x_scale, const void *wq,
+                               const float *w_scale, const void *bias, int bias_dtype,
+                               void *out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                               void *stream);
+
+/*
+ * Device workspace fp8lin_fp8_linear needs for M tokens of width K: the e4m3 codes
+ * and the per-token scales of x (aligned sub-buffers).
+ */
+FP8LIN_API size_t fp8lin_linear_workspace_size(int64_t M, int64_t K);
+
+/*
+ * Fused dynamic-quant FP8 linear: fp8lin_quantize_fp8 then fp8lin_fp8_gemm, the
+ * GEMM launched as a programmatic dependent of the quantizer so its prologue
+ * overlaps the quantizer's tail.
+ * Replaces fp8_linear's per-channel branch (csrc/fp8_gemm.cu:196-221). The caller
+ * flattens x's leading dimensions into M (the reference's x.reshape(-1, K)).
+ *   x [M,K] (BF16/F16); wq/w_scale/bias as in fp8lin_fp8_gemm; out [M,N] out_dtype
+ *   workspace: >= fp8lin_linear_workspace_size(M, K) bytes of device memory,
+ *   256-byte aligned, owned by the caller and reusable after the call's stream
+ *   work completes.
+ */
+FP8LIN_API int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq,
+                                 const float *w_scale, const void *bias, int bias_dtype,
+                                 void *out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                 void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Watchdog status of the GEMM kernel on the current device: every wait in the
+ * kernel is bounded; a wait that runs out sets a bit here and the kernel returns
+ * early instead of hanging (1 = TMA producer, 2 = MMA issuer, 4 = epilogue).
+ * *status receives the bits; clear != 0 resets them. Synchronous on the device.
+ * No counterpart in the reference (cuBLASLt has no such report).
+ */
+FP8LIN_API int fp8lin_device_status(unsigned int *status, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP8LINEAR_B200_H */

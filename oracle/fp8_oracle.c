@@ -1,0 +1,219 @@
+/*
+ * fp8_oracle.c -- CPU restatement of drbh/fp8linear's per-channel FP8 linear path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the checker that the CUDA kernels of
+ * fp8linear_b200 are compared against; it is never linked into, called by or
+ * shipped with the product. Only tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline leg load it (through oracle/oracle.py).
+ *
+ * Each function restates one piece of the reference (paths relative to the
+ * reference project root):
+ *   oracle_e4m3_encode      __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3)
+ *                           (csrc/quantize.cu:71) and c10::Float8_e4m3fn's
+ *                           non-saturating cast (csrc/quantize.cu:364)
+ *   oracle_quantize_rows    quant_rowwise_kernel + block_reduce_max
+ *                           (csrc/quantize.cu:28-73), launched by quantize_fp8
+ *                           (csrc/quantize.cu:199-234)
+ *   oracle_quantize_weight  per-channel branch of quantize_weight
+ *                           (csrc/quantize.cu:359-365), as ATen evaluates it on CUDA
+ *   oracle_gemm_dequant     cuBLASLt unscaled e4m3 matmul (csrc/fp8_gemm.cu:109-131,
+ *                           180-184) followed by dequant_bias_kernel
+ *                           (csrc/fp8_gemm.cu:65-80)
+ *
+ * Arithmetic is IEEE binary32 with round-to-nearest-even and no flush-to-zero,
+ * which is what nvcc emits for the reference without --use_fast_math.
+ * Build: cc -O2 -fPIC -shared -ffp-contract=off -fno-fast-math fp8_oracle.c -o liboracle.so
+ * (-ffp-contract=off keeps x*inv and (acc*xs)*ws as separate roundings.)
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#define E4M3_MAX 448.0f
+
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* bf16 / fp16 storage -> fp32 (exact). */
+float oracle_bf16_to_f32(uint16_t h) { return u2f(((uint32_t)h) << 16); }
+
+float oracle_f16_to_f32(uint16_t h) {
+  uint32_t s = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t e = (h >> 10) & 0x1f;
+  uint32_t m = h & 0x3ffu;
+  if (e == 0) {
+    /* zero or subnormal: m * 2^-24 is exact in fp32 */
+    float v = (float)m * u2f(0x33800000u); /* 2^-24 */
+    return s ? -v : v;
+  }
+  if (e == 31) return u2f(s | 0x7f800000u | (m << 13));
+  return u2f(s | ((e + 112u) << 23) | (m << 13));
+}
+
+/* fp32 -> fp16 storage, round-to-nearest-even (IEEE __float2half_rn). */
+uint16_t oracle_f32_to_f16(float f) {
+  uint32_t u = f2u(f);
+  uint16_t s = (uint16_t)((u >> 16) & 0x8000u);
+  uint32_t a = u & 0x7fffffffu;
+  if (a >= 0x7f800000u) return (uint16_t)(s | 0x7c00u | (a > 0x7f800000u ? 0x200u : 0));
+  float af = u2f(a);
+  if (af >= 65520.0f) return (uint16_t)(s | 0x7c00u); /* rounds to inf */
+  if (af < 6.103515625e-05f) {                         /* below 2^-14: subnormal */
+    float q = rintf(af * 16777216.0f);                   /* units of 2^-24, RNE */
+    return (uint16_t)(s | (uint16_t)q);                  /* q==1024 -> smallest normal */
+  }
+  uint32_t e = (a >> 23) - 112u;
+  uint32_t m = a & 0x7fffffu;
+  uint32_t keep = m >> 13, rem = m & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (keep & 1u))) keep++;
+  if (keep == 0x400u) { keep = 0; e++; }
+  return (uint16_t)(s | (e << 10) | keep);
+}
+
+/*
+ * fp32 -> e4m3fn byte, round-to-nearest-even.
+ * saturate != 0: finite magnitudes above 448 clamp to 448 and NaN gives 0x7F
+ *                (the __NV_SATFINITE hardware convert).
+ * saturate == 0: magnitudes that round above 448 (>= 464) and NaN give NaN with
+ *                the input's sign (c10::Float8_e4m3fn's software cast).
+ */
+uint8_t oracle_e4m3_encode(float v, int saturate) {
+  uint32_t u = f2u(v);
+  uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+  uint32_t a = u & 0x7fffffffu;
+  if (a > 0x7f800000u) return saturate ? 0x7f : (uint8_t)(sign | 0x7f);
+  float af = u2f(a);
+  if (af >= 464.0f) { /* includes +inf */
+    if (saturate) return (uint8_t)(sign | 0x7e);
+    return (uint8_t)(sign | 0x7f);
+  }
+  if (af > E4M3_MAX) /* (448, 464): rounds to 448 under RNE (480 is not a finite code) */
+    return (uint8_t)(sign | 0x7e);
+  if (af < 0.015625f) { /* below 2^-6: subnormal grid of 2^-9 */
+    float q = rintf(af * 512.0f); /* exact scale, RNE to integer 0..8 */
+    return (uint8_t)(sign | (uint8_t)q); /* q == 8 encodes 2^-6 (exp 1, mant 0) */
+  }
+  int e = (int)(a >> 23) - 127; /* -6 .. 8 */
+  uint32_t m = a & 0x7fffffu;
+  uint32_t keep = m >> 20, rem = m & 0xfffffu;
+  if (rem > 0x80000u || (rem == 0x80000u && (keep & 1u))) keep++;
+  if (keep == 8u) { keep = 0; e++; }
+  return (uint8_t)(sign | (uint8_t)((e + 7) << 3) | (uint8_t)keep);
+}
+
+float oracle_e4m3_decode(uint8_t b) {
+  uint32_t s = b & 0x80u;
+  uint32_t e = (b >> 3) & 0xfu;
+  uint32_t m = b & 7u;
+  float v;
+  if (e == 15 && m == 7) return u2f(0x7fc00000u | (s << 24));
+  if (e == 0) v = (float)m * 0.001953125f; /* m * 2^-9 */
+  else v = u2f(((e + 120u) << 23) | (m << 20));
+  return s ? -v : v;
+}
+
+/*
+ * Per-token quantization, csrc/quantize.cu:45-73.
+ *   amax = fmaxf-reduce |x| (NaN inputs are ignored by fmaxf; quantize.cu:52-55)
+ *   sc   = fmaxf(amax / 448, 1e-12)  (IEEE divide; quantize.cu:60)
+ *   inv  = 1 / sc                    (quantize.cu:62)
+ *   q    = e4m3_satfinite(fminf(fmaxf(x * inv, -448), 448))  (quantize.cu:69-71)
+ * dtype 0 = bf16 input, 1 = fp16 input.
+ */
+void oracle_quantize_rows(const uint16_t *x, int dtype, int64_t M, int64_t K,
+                          uint8_t *xq, float *scale) {
+  for (int64_t r = 0; r < M; ++r) {
+    const uint16_t *row = x + r * K;
+    float amax = 0.0f;
+    for (int64_t j = 0; j < K; ++j) {
+      float v = dtype ? oracle_f16_to_f32(row[j]) : oracle_bf16_to_f32(row[j]);
+      amax = fmaxf(amax, fabsf(v));
+    }
+    volatile float sc = fmaxf(amax / E4M3_MAX, 1e-12f);
+    volatile float inv = 1.0f / sc;
+    scale[r] = sc;
+    for (int64_t j = 0; j < K; ++j) {
+      float v = dtype ? oracle_f16_to_f32(row[j]) : oracle_bf16_to_f32(row[j]);
+      volatile float p = v * inv;
+      float c = fminf(fmaxf(p, -E4M3_MAX), E4M3_MAX);
+      xq[r * K + j] = oracle_e4m3_encode(c, 1);
+    }
+  }
+}
+
+/*
+ * Per-channel weight quantization, csrc/quantize.cu:360-364, as ATen runs it on CUDA:
+ *   amax  = |w|.amax(1).float()        (NaN propagates through amax)
+ *   scale = (amax / 448).clamp_min(1e-12)
+ *           ATen's CUDA true-divide by a host scalar multiplies by the fp32
+ *           reciprocal: amax * (1.0f / 448.0f). recip_scalar != 0 selects that;
+ *           0 selects a true division (ATen's CPU kernel).
+ *   wq    = (w.float() / scale[:,None]).clamp(-448, 448).to(float8_e4m3fn)
+ *           (true division; clamp and the cast propagate NaN; the cast does not
+ *           saturate).
+ * dtype 0 = bf16 input, 1 = fp16 input, 2 = fp32 input.
+ */
+void oracle_quantize_weight(const void *w, int dtype, int64_t N, int64_t K,
+                            int recip_scalar, uint8_t *wq, float *scale) {
+  const uint16_t *w16 = (const uint16_t *)w;
+  const float *w32 = (const float *)w;
+  const float inv448 = 1.0f / E4M3_MAX;
+  for (int64_t r = 0; r < N; ++r) {
+    float amax = 0.0f;
+    int has_nan = 0;
+    for (int64_t j = 0; j < K; ++j) {
+      float v = dtype == 2 ? w32[r * K + j]
+                : dtype == 1 ? oracle_f16_to_f32(w16[r * K + j])
+                             : oracle_bf16_to_f32(w16[r * K + j]);
+      float a = fabsf(v);
+      if (a != a) has_nan = 1;
+      else if (a > amax) amax = a;
+    }
+    volatile float s;
+    if (has_nan) s = u2f(0x7fffffffu);
+    else if (recip_scalar) s = amax * inv448;
+    else s = amax / E4M3_MAX;
+    float sc = (s != s) ? s : (s < 1e-12f ? 1e-12f : s);
+    scale[r] = sc;
+    for (int64_t j = 0; j < K; ++j) {
+      float v = dtype == 2 ? w32[r * K + j]
+                : dtype == 1 ? oracle_f16_to_f32(w16[r * K + j])
+                             : oracle_bf16_to_f32(w16[r * K + j]);
+      volatile float q = v / sc;
+      float c = q;
+      if (c == c) c = c < -E4M3_MAX ? -E4M3_MAX : (c > E4M3_MAX ? E4M3_MAX : c);
+      wq[r * K + j] = oracle_e4m3_encode(c, 0);
+    }
+  }
+}
+
+/*
+ * acc[m,n] = sum_k e4m3(xq[m,k]) * e4m3(wq[n,k])   (csrc/fp8_gemm.cu:109-131, 180-184;
+ *            products of two e4m3 values are exact in fp32, the sum is taken in
+ *            double here and rounded once, i.e. the exact-sum limit of any fp32
+ *            accumulation order)
+ * out[m,n] = (acc * xs[m]) * ws[n] + float(bias16[n])   (csrc/fp8_gemm.cu:75-77)
+ * bias16 is the bias already rounded to fp16 (csrc/fp8_gemm.cu:171), or NULL.
+ * round_out != 0 rounds out to fp16 like csrc/fp8_gemm.cu:78 (returned widened to fp32).
+ */
+void oracle_gemm_dequant(const uint8_t *xq, const float *xs, const uint8_t *wq,
+                         const float *ws, const uint16_t *bias16, int64_t M,
+                         int64_t N, int64_t K, int round_out, float *acc_out,
+                         float *out) {
+  float lut[256];
+  for (int i = 0; i < 256; ++i) lut[i] = oracle_e4m3_decode((uint8_t)i);
+  for (int64_t m = 0; m < M; ++m) {
+    const uint8_t *a = xq + m * K;
+    for (int64_t n = 0; n < N; ++n) {
+      const uint8_t *b = wq + n * K;
+      double s = 0.0;
+      for (int64_t k = 0; k < K; ++k) s += (double)lut[a[k]] * (double)lut[b[k]];
+      float acc = (float)s;
+      if (acc_out) acc_out[m * N + n] = acc;
+      volatile float t = acc * xs[m];
+      volatile float v = t * ws[n];
+      if (bias16) v = v + oracle_f16_to_f32(bias16[n]);
+      out[m * N + n] = round_out ? oracle_f16_to_f32(oracle_f32_to_f16(v)) : v;
+    }
+  }
+}

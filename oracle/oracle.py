@@ -1,0 +1,289 @@
+"""CPU oracle for the per-channel FP8 linear path of drbh/fp8linear.
+
+TEST INFRASTRUCTURE ONLY: the checker for fp8linear_b200's CUDA kernels. Only
+``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
+import it. The product package never imports anything under ``oracle/``.
+
+Two restatements of the same algorithm live here:
+
+* ``C`` -- ``fp8_oracle.c`` through ctypes: scalar, one element at a time, the
+  primary restatement (see the citations in that file).
+* ``np_*`` / ``port_*`` -- vectorised numpy/torch versions of the same steps, used
+  at sizes where the scalar code would take too long and as the timed CPU
+  baseline (the "torch emulation" CPU path: per-token e4m3 quant, fp32 matmul of
+  the codes, dequant + bias). Tests check them against the C restatement.
+
+Reference citations (paths relative to the reference project root):
+  activation quant     csrc/quantize.cu:45-73 (kernel), :199-234 (host op)
+  weight quant         csrc/quantize.cu:359-365
+  GEMM + dequant/bias  csrc/fp8_gemm.cu:139-194, dequant_bias_kernel :65-80
+  fused entry          csrc/fp8_gemm.cu:196-221
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+SRC = HERE / "fp8_oracle.c"
+BUILD_DIR = HERE / "_build"
+LIB_PATH = BUILD_DIR / "liboracle.so"
+
+E4M3_MAX = np.float32(448.0)
+SCALE_FLOOR = np.float32(1e-12)
+BF16, F16, F32 = 0, 1, 2
+
+
+# ----------------------------------------------------------------------------- build
+
+
+def build() -> Path:
+    """Compile fp8_oracle.c into oracle/_build/liboracle.so (skipped when fresh)."""
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    if LIB_PATH.exists() and LIB_PATH.stat().st_mtime >= SRC.stat().st_mtime:
+        return LIB_PATH
+    tmp = LIB_PATH.with_suffix(f".so.{os.getpid()}")
+    cmd = ["cc", "-O2", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
+           "-std=c11", str(SRC), "-o", str(tmp), "-lm"]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        path = build()
+        L = ctypes.CDLL(str(path))
+        P = ctypes.c_void_p
+        i64 = ctypes.c_int64
+        L.oracle_e4m3_encode.argtypes = [ctypes.c_float, ctypes.c_int]
+        L.oracle_e4m3_encode.restype = ctypes.c_uint8
+        L.oracle_e4m3_decode.argtypes = [ctypes.c_uint8]
+        L.oracle_e4m3_decode.restype = ctypes.c_float
+        L.oracle_quantize_rows.argtypes = [P, ctypes.c_int, i64, i64, P, P]
+        L.oracle_quantize_rows.restype = None
+        L.oracle_quantize_weight.argtypes = [P, ctypes.c_int, i64, i64, ctypes.c_int, P, P]
+        L.oracle_quantize_weight.restype = None
+        L.oracle_gemm_dequant.argtypes = [P, P, P, P, P, i64, i64, i64, ctypes.c_int, P, P]
+        L.oracle_gemm_dequant.restype = None
+        L.oracle_f32_to_f16.argtypes = [ctypes.c_float]
+        L.oracle_f32_to_f16.restype = ctypes.c_uint16
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ----------------------------------------------------------------------------- C restatement
+
+
+def c_quantize_rows(x16: np.ndarray, dtype: int = BF16):
+    """x16: uint16 [M, K] holding bf16 (dtype 0) or fp16 (dtype 1) bit patterns."""
+    x16 = np.ascontiguousarray(x16, dtype=np.uint16)
+    M, K = x16.shape
+    xq = np.empty((M, K), np.uint8)
+    sc = np.empty((M,), np.float32)
+    lib().oracle_quantize_rows(_ptr(x16), dtype, M, K, _ptr(xq), _ptr(sc))
+    return xq, sc
+
+
+def c_quantize_weight(w: np.ndarray, dtype: int = BF16, recip_scalar: bool = True):
+    """w: uint16 bit patterns (bf16/fp16) or float32 [N, K]."""
+    w = np.ascontiguousarray(w)
+    N, K = w.shape
+    wq = np.empty((N, K), np.uint8)
+    sc = np.empty((N,), np.float32)
+    lib().oracle_quantize_weight(_ptr(w), dtype, N, K, int(recip_scalar), _ptr(wq), _ptr(sc))
+    return wq, sc
+
+
+def c_gemm_dequant(xq, xs, wq, ws, bias16=None, round_out=True, want_acc=False):
+    xq = np.ascontiguousarray(xq, np.uint8)
+    wq = np.ascontiguousarray(wq, np.uint8)
+    xs = np.ascontiguousarray(xs, np.float32)
+    ws = np.ascontiguousarray(ws, np.float32)
+    if bias16 is not None:
+        bias16 = np.ascontiguousarray(bias16, np.uint16)
+    M, K = xq.shape
+    N = wq.shape[0]
+    out = np.empty((M, N), np.float32)
+    acc = np.empty((M, N), np.float32) if want_acc else None
+    lib().oracle_gemm_dequant(_ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws), _ptr(bias16),
+                              M, N, K, int(round_out), _ptr(acc), _ptr(out))
+    return (out, acc) if want_acc else out
+
+
+def c_e4m3_encode(v: float, saturate: bool = True) -> int:
+    return int(lib().oracle_e4m3_encode(float(v), int(saturate)))
+
+
+# ----------------------------------------------------------------------------- numpy port
+
+
+def bf16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return (h.astype(np.uint32) << 16).view(np.float32)
+
+
+def f16_bits_to_f32(h: np.ndarray) -> np.ndarray:
+    return h.view(np.float16).astype(np.float32)
+
+
+def f32_to_bf16_bits(f: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bit patterns (NaN kept quiet)."""
+    u = np.ascontiguousarray(f, np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r = np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+    return r
+
+
+def np_e4m3_encode(v: np.ndarray, saturate: bool = True) -> np.ndarray:
+    """Vectorised twin of oracle_e4m3_encode (RNE, same saturate semantics)."""
+    v = np.ascontiguousarray(v, np.float32)
+    u = v.view(np.uint32)
+    sign = ((u >> 24) & 0x80).astype(np.uint8)
+    a_bits = u & np.uint32(0x7FFFFFFF)
+    af = a_bits.view(np.float32)
+    # normal path
+    e = (a_bits >> 23).astype(np.int32) - 127
+    m = a_bits & np.uint32(0x7FFFFF)
+    keep = (m >> 20).astype(np.int32)
+    rem = m & np.uint32(0xFFFFF)
+    up = (rem > 0x80000) | ((rem == 0x80000) & ((keep & 1) == 1))
+    keep = keep + up.astype(np.int32)
+    carry = keep == 8
+    keep = np.where(carry, 0, keep)
+    e = e + carry.astype(np.int32)
+    normal = (((e + 7) << 3) | keep).astype(np.int32)
+    # subnormal path (below 2^-6)
+    with np.errstate(invalid="ignore", over="ignore"):
+        sub = np.rint(af * np.float32(512.0))
+        sub = np.where(np.isfinite(sub), sub, 0).astype(np.int32)
+    code = np.where(af < np.float32(0.015625), sub, normal)
+    code = np.where(af > E4M3_MAX, 0x7E, code)
+    big = af >= np.float32(464.0)
+    nan = a_bits > 0x7F800000
+    if saturate:
+        code = np.where(big, 0x7E, code)
+        res = (code.astype(np.uint8) | sign)
+        res = np.where(nan, np.uint8(0x7F), res)
+    else:
+        code = np.where(big | nan, 0x7F, code)
+        res = code.astype(np.uint8) | sign
+    return res.astype(np.uint8)
+
+
+_DECODE_LUT = None
+
+
+def e4m3_decode_lut() -> np.ndarray:
+    global _DECODE_LUT
+    if _DECODE_LUT is None:
+        b = np.arange(256, dtype=np.uint32)
+        s = (b & 0x80) != 0
+        e = (b >> 3) & 0xF
+        m = b & 7
+        sub = m.astype(np.float32) * np.float32(2.0 ** -9)
+        nrm = ((e + 120) << 23 | (m << 20)).astype(np.uint32).view(np.float32)
+        v = np.where(e == 0, sub, nrm).astype(np.float32)
+        v = np.where((e == 15) & (m == 7), np.float32(np.nan), v)
+        _DECODE_LUT = np.where(s, -v, v).astype(np.float32)
+    return _DECODE_LUT
+
+
+def np_quantize_rows(x16: np.ndarray, dtype: int = BF16):
+    """Vectorised twin of oracle_quantize_rows (bit-identical)."""
+    x16 = np.ascontiguousarray(x16, np.uint16)
+    xf = bf16_bits_to_f32(x16) if dtype == BF16 else f16_bits_to_f32(x16)
+    if xf.shape[0] == 0:
+        return np.empty(xf.shape, np.uint8), np.empty((0,), np.float32)
+    amax = np.fmax.reduce(np.abs(xf), axis=1, initial=np.float32(0.0)).astype(np.float32)
+    sc = np.fmax(amax / E4M3_MAX, SCALE_FLOOR).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        inv = (np.float32(1.0) / sc).astype(np.float32)
+        p = (xf * inv[:, None]).astype(np.float32)
+    c = np.fmin(np.fmax(p, -E4M3_MAX), E4M3_MAX)
+    return np_e4m3_encode(c, saturate=True), sc
+
+
+def np_quantize_weight(w: np.ndarray, dtype: int = BF16, recip_scalar: bool = True):
+    """Vectorised twin of oracle_quantize_weight (bit-identical, NaN sign aside)."""
+    if dtype == F32:
+        wf = np.ascontiguousarray(w, np.float32)
+    else:
+        w16 = np.ascontiguousarray(w, np.uint16)
+        wf = bf16_bits_to_f32(w16) if dtype == BF16 else f16_bits_to_f32(w16)
+    a = np.abs(wf)
+    amax = np.max(a, axis=1, initial=np.float32(0.0)).astype(np.float32)  # NaN propagates
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        if recip_scalar:
+            s = (amax * (np.float32(1.0) / E4M3_MAX)).astype(np.float32)
+        else:
+            s = (amax / E4M3_MAX).astype(np.float32)
+        sc = np.where(np.isnan(s), s, np.maximum(s, SCALE_FLOOR)).astype(np.float32)
+        q = (wf / sc[:, None]).astype(np.float32)
+    c = np.where(np.isnan(q), q, np.clip(q, -E4M3_MAX, E4M3_MAX)).astype(np.float32)
+    return np_e4m3_encode(c, saturate=False), sc
+
+
+def port_gemm_dequant(xq, xs, wq, ws, bias16=None, round_out=True, acc_dtype="float64",
+                      threads: int | None = None):
+    """Vectorised twin of oracle_gemm_dequant; the matmul runs in torch on the CPU.
+
+    acc_dtype "float64" gives the exact-sum reference (tests); "float32" is the
+    reference's own fp32-accumulate arithmetic (the timed CPU baseline).
+    """
+    import torch
+
+    if threads is not None:
+        torch.set_num_threads(threads)
+    lut = torch.from_numpy(e4m3_decode_lut())
+    tdt = torch.float64 if acc_dtype == "float64" else torch.float32
+    a = lut[torch.from_numpy(np.ascontiguousarray(xq, np.uint8)).long()].to(tdt)
+    b = lut[torch.from_numpy(np.ascontiguousarray(wq, np.uint8)).long()].to(tdt)
+    acc = (a @ b.T).to(torch.float32)
+    t = acc * torch.from_numpy(np.ascontiguousarray(xs, np.float32))[:, None]
+    v = t * torch.from_numpy(np.ascontiguousarray(ws, np.float32))[None, :]
+    if bias16 is not None:
+        bh = torch.from_numpy(np.ascontiguousarray(bias16, np.uint16).view(np.float16))
+        v = v + bh.float()[None, :]
+    if round_out:
+        v = v.half().float()
+    return v.numpy()
+
+
+def port_linear(x16: np.ndarray, wq, ws, bias16=None, dtype: int = BF16, acc_dtype="float32",
+                round_out=True):
+    """Whole reference CPU path (fp8_linear, csrc/fp8_gemm.cu:196-221) on a 2-D x."""
+    xq, xs = np_quantize_rows(x16, dtype)
+    return port_gemm_dequant(xq, xs, wq, ws, bias16, round_out=round_out, acc_dtype=acc_dtype)
+
+
+# ----------------------------------------------------------------------------- checks
+
+
+def max_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
+    """max|got - ref| / max|ref| in fp32 (the tolerance measure for outputs)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    denom = np.max(np.abs(ref)) if ref.size else 0.0
+    if ref.size == 0:
+        return 0.0
+    return float(np.max(np.abs(got - ref)) / max(denom, 1e-30))
+
+
+def norm_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
+    """||got - ref|| / ||ref|| (the measure scripts/mxfp8_check.py:62 prints)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))

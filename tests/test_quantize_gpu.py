@@ -1,0 +1,137 @@
+"""Per-token quantizer on the GPU: e4m3 codes and fp32 scales bit-exact against the
+CPU oracle (oracle/fp8_oracle.c restating csrc/quantize.cu:45-73), against a full-size
+torch restatement, and against the reference's own compiled kernel when present."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from fp8linear_b200.workloads import WORKLOADS, make_x
+from tests.helpers import bits16, codes, require_sm100, torch_quant_ref, u32
+
+pytestmark = pytest.mark.gpu
+
+ALL = list(WORKLOADS)
+ORACLE_ROWS = 1024  # rows checked against the scalar C oracle per workload
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _dev():
+    require_sm100()
+    import fp8linear_b200  # noqa: F401
+
+
+def _rows(M: int, n: int, seed: int = 0) -> np.ndarray:
+    if M <= n:
+        return np.arange(M)
+    return np.sort(np.random.default_rng(seed).choice(M, n, replace=False))
+
+
+@pytest.mark.parametrize("name", ALL)
+def test_quantize_workloads_bitexact(name, oracle):
+    from fp8linear_b200 import ops
+
+    wl = WORKLOADS[name]
+    x = make_x(wl, gen_device="cuda")
+    xq, xs = ops.quantize_fp8(x)
+    torch.cuda.synchronize()
+    # full size: torch restatement on the GPU
+    tq, ts = torch_quant_ref(x)
+    assert torch.equal(xq.view(torch.uint8), tq.view(torch.uint8))
+    assert torch.equal(xs.view(torch.int32), ts.view(torch.int32))
+    # row sample: scalar C oracle
+    rows = _rows(wl.M, ORACLE_ROWS)
+    sel = torch.from_numpy(rows).cuda()
+    oq, osc = oracle.c_quantize_rows(bits16(x[sel]), oracle.BF16)
+    assert np.array_equal(codes(xq[sel]), oq)
+    assert np.array_equal(u32(xs[sel]), osc.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("K", [16, 24, 40, 64, 100, 1000, 1024, 3072, 4104, 12288, 15360, 65536, 70000])
+def test_quantize_shapes_vs_oracle(K, dtype, oracle):
+    from fp8linear_b200 import ops
+
+    M = 37
+    g = torch.Generator(device="cpu").manual_seed(K)
+    x = (torch.randn(M, K, generator=g) * torch.logspace(-3, 2, M)[:, None]).to(dtype).cuda()
+    xq, xs = ops.quantize_fp8(x)
+    oq, osc = oracle.c_quantize_rows(bits16(x), 0 if dtype == torch.bfloat16 else 1)
+    assert np.array_equal(codes(xq), oq)
+    assert np.array_equal(u32(xs), osc.view(np.uint32))
+
+
+def test_quantize_edge_values(oracle):
+    """Zero rows, exact 448, e4m3 midpoints, subnormals, -0.0, inf and NaN inputs."""
+    from fp8linear_b200 import ops
+
+    K = 64
+    lut = oracle.e4m3_decode_lut()
+    fin = lut[np.isfinite(lut)]
+    mids = ((fin[:-1] + fin[1:]) / 2).astype(np.float32)
+    rows = [
+        np.zeros(K, np.float32),                                   # all zero -> scale 1e-12
+        np.full(K, -0.0, np.float32),                              # negative zeros
+        np.concatenate([[448.0], np.linspace(-448, 448, K - 1)]),  # amax exactly 448
+        np.resize(np.sort(np.abs(mids))[:K], K),                   # e4m3 midpoints
+        np.resize(np.array([2.0 ** -10, 3 * 2.0 ** -10, 2.0 ** -9, 448.0]), K),  # subnormals
+        np.resize(np.array([np.inf, 1.0, -2.0, 0.5]), K),          # inf amax -> inv 0
+        np.resize(np.array([np.nan, 1.0, -3.0, 0.25]), K),         # NaN ignored by fmaxf
+        np.resize(np.array([-np.inf, np.nan, 5.0, -5.0]), K),
+        np.full(K, 1e-30, np.float32),                             # tiny row (bf16 rounds)
+    ]
+    xf = torch.from_numpy(np.stack(rows).astype(np.float32))
+    for dtype, code in ((torch.bfloat16, 0), (torch.float16, 1)):
+        x = xf.to(dtype).cuda()
+        xq, xs = ops.quantize_fp8(x)
+        oq, osc = oracle.c_quantize_rows(bits16(x), code)
+        assert np.array_equal(codes(xq), oq), dtype
+        assert np.array_equal(u32(xs), osc.view(np.uint32)), dtype
+
+
+def test_quantize_empty_and_one_row():
+    from fp8linear_b200 import ops
+
+    x = torch.empty(0, 3072, dtype=torch.bfloat16, device="cuda")
+    xq, xs = ops.quantize_fp8(x)
+    assert xq.shape == (0, 3072) and xs.shape == (0,)
+    x = torch.randn(1, 3072, device="cuda").bfloat16()
+    xq, xs = ops.quantize_fp8(x)
+    tq, ts = torch_quant_ref(x)
+    assert torch.equal(xq.view(torch.uint8), tq.view(torch.uint8))
+
+
+def test_quantize_strided_input():
+    """A non-contiguous / offset view is made contiguous first, like the reference."""
+    from fp8linear_b200 import ops
+
+    base = torch.randn(64, 3072 + 8, device="cuda").bfloat16()
+    x = base[:, 4:3076]
+    xq, xs = ops.quantize_fp8(x)
+    tq, ts = torch_quant_ref(x.contiguous())
+    assert torch.equal(xq.view(torch.uint8), tq.view(torch.uint8))
+
+
+@pytest.mark.parametrize("name", ["small_cpu", "flux_qkv", "flux_fc2", "sweep_M16"])
+def test_quantize_matches_reference_kernel(name, ref_ops):
+    if ref_ops is None:
+        pytest.skip("reference ops not built (oracle/_ref)")
+    from fp8linear_b200 import ops
+
+    wl = WORKLOADS[name]
+    x = make_x(wl, gen_device="cuda")
+    xq, xs = ops.quantize_fp8(x)
+    rq, rs = ref_ops.quantize_fp8(x)
+    assert torch.equal(xq.view(torch.uint8), rq.view(torch.uint8))
+    assert torch.equal(xs.view(torch.int32), rs.view(torch.int32))
+
+
+def test_quantize_capi_matches_op(capi):
+    from fp8linear_b200 import ops
+
+    x = make_x(WORKLOADS["flux_qkv"], gen_device="cuda")
+    a = ops.quantize_fp8(x)
+    b = capi.quantize_fp8(x)
+    assert torch.equal(a[0].view(torch.uint8), b[0].view(torch.uint8))
+    assert torch.equal(a[1], b[1])
