@@ -1,0 +1,469 @@
+"""Benchmark of the fused FP8 linear hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+A step is one ``fp8_linear`` over one batch of synthetic FLUX-shaped activations:
+per-token e4m3 quantization of x (bf16), the tcgen05 FP8 GEMM against a per-channel
+e4m3 weight with the dequant + bias epilogue fused in, bf16 out. The default workload
+is the FLUX double-block QKV linear (M=4608 tokens, K=3072 -> N=9216).
+
+Multi-GPU (torchrun, one process per GPU): token rows shard with the weight
+replicated and no collective; each rank runs its own M-row batch (weak scaling) and
+``value`` is the FLOPs of all ranks over the max-over-ranks device time.
+
+Timing: W untimed warm-up steps, then exactly K timed steps between a barrier and a
+device synchronize; each step is bracketed by CUDA events on the launching stream and
+a 256 MiB buffer is written between steps (more than the 126 MB L2), so every step
+reads its operands from HBM. ``e2e`` repeats the step through the C ABI with the
+activations copied from pinned host memory and the output copied back inside the
+timed region. ``roofline`` times the GEMM kernel alone over K further launches.
+``cpu_baseline`` times the CPU restatement of the reference path (the oracle port:
+per-token e4m3 quant, fp32 matmul, dequant + bias) on a bounded row sample.
+
+``--impl reference`` times the reference's path on the host CPU instead (the oracle
+port, all host threads) and, when the reference's own CUDA ops were compiled into
+oracle/_ref, reports their device time on the same workload as ``gpu_reference``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP8 linear TFLOP/s at FLUX shapes vs 4.5 PF peak; quant GB/s vs 8 TB/s"
+FLUSH_BYTES = 256 << 20
+NOMINAL_FP8_TFLOPS = 4500.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+# ----------------------------------------------------------------------------- plumbing
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    return {**FALLBACK, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return self
+
+        def pump():
+            for line in self.proc.stdout:
+                self.rows.append([c.strip() for c in line.split(",")])
+
+        self._t = threading.Thread(target=pump, daemon=True)
+        self._t.start()
+        return self
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                power.append(float(r[3]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------------------- CPU path
+
+
+def cpu_reference_runner(wl, rows: int, threads: int | None = None):
+    """The reference path on the CPU (oracle port) for ``rows`` token rows of ``wl``.
+
+    The weight is quantized once (offline, as the reference's quantize_weight) and kept
+    decoded to fp32; each call quantizes x per token, decodes the codes, runs the fp32
+    matmul and applies (acc * xs) * ws + bias.
+    """
+    import numpy as np
+    from oracle import oracle as O
+    from fp8linear_b200.workloads import make_weight, make_x
+
+    if threads:
+        torch.set_num_threads(threads)
+    x = make_x(wl, M=rows, seed=7)
+    w, b = make_weight(wl)
+    w16 = w.contiguous().view(torch.int16).numpy().view(np.uint16)
+    wq, ws = O.np_quantize_weight(w16, O.BF16)
+    lut = torch.from_numpy(O.e4m3_decode_lut())
+    wf = lut[torch.from_numpy(wq).long()]
+    wsv = torch.from_numpy(ws)
+    bias = b.float()
+    x16 = x.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    def step():
+        xq, xs = O.np_quantize_rows(x16, O.BF16)
+        a = lut[torch.from_numpy(xq).long()]
+        acc = a @ wf.T
+        return (acc * torch.from_numpy(xs)[:, None]) * wsv[None, :] + bias[None, :]
+
+    return step
+
+
+def time_cpu(step, min_seconds: float = 3.0, max_iters: int = 1000):
+    step()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or n >= max_iters:
+            return el / n, n
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+
+def run_gpu(args):
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    import fp8linear_b200 as f
+    from fp8linear_b200.capi import CApi
+    from fp8linear_b200.workloads import WORKLOADS, make_weight, make_x
+
+    wl = WORKLOADS[args.workload]
+    M, K, N = wl.M, wl.K, wl.N
+    x = make_x(wl, seed=rank, gen_device="cuda")          # this rank's shard of token rows
+    w, b = make_weight(wl, gen_device="cuda")              # replicated weight
+    wq, ws = f.quantize_weight(w)
+    del w
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return f.fp8_linear(x, wq, ws, b)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    barrier()
+
+    # ---- timed: K fused steps, L2 flushed between steps
+    clocks = ClockSampler(local).start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    barrier()
+    clk = clocks.stop()
+    step_ms = [a.elapsed_time(b_) for a, b_ in ev]
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    flops_rank = wl.flops
+    value = world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12
+    ms_per_step = total_ms / args.steps
+
+    # ---- roofline: GEMM kernel and quantizer timed alone (same stream, events per launch)
+    xq, xs = f.quantize_fp8(x)
+    gemm_ms, quant_ms = [], []
+    for i in range(args.steps):
+        flush.zero_()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        f.quantize_fp8(x)
+        e1.record(stream)
+        flush.zero_()
+        e1b = torch.cuda.Event(enable_timing=True)
+        e1b.record(stream)
+        f.fp8_gemm(xq, xs, wq, ws, b)
+        e2.record(stream)
+        gemm_ms.append((e1b, e2))
+        quant_ms.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    g_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in gemm_ms)
+    q_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in quant_ms)
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    gemm_tflops = flops_rank / (g_ms * 1e-3) / 1e12
+    quant_gbs = wl.quant_bytes / (q_ms * 1e-3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / f"traffic_{args.workload}.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("gemm_dram_bytes_per_launch")
+
+    # ---- e2e through the C ABI with host buffers (H2D x, linear, D2H out), timed
+    capi = CApi()
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    out_dev = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    wsz = capi.workspace_size(M, K)
+    work = torch.empty(wsz, dtype=torch.uint8, device=dev)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        capi.fp8_linear(x_dev, wq, ws, b, out=out_dev, workspace=work)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e2e_ev = []
+    for i in range(args.steps):
+        flush.zero_()
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_step()
+        c.record(stream)
+        e2e_ev.append((a, c))
+    barrier()
+    e2e_total = sum(a.elapsed_time(c) for a, c in e2e_ev)
+    if world > 1:
+        t = torch.tensor([e2e_total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = world * flops_rank * args.steps / (e2e_total * 1e-3) / 1e12
+
+    status = capi.device_status()
+
+    # ---- CPU baseline (rank 0, N=1 only): oracle port on a bounded row sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rows = args.cpu_rows
+        st = cpu_reference_runner(wl, rows)
+        per, n = time_cpu(st, min_seconds=args.cpu_seconds)
+        cpu = {"value": 2 * rows * N * K / per / 1e12, "unit": "TFLOP/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{rows} of {M} token rows of {wl.name} (K={K}, N={N}), {n} passes, "
+                         f"{per * 1e3:.1f} ms/pass; fp32 torch matmul of decoded e4m3 codes",
+               "host_cpus": os.cpu_count()}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "e4m3",
+            "data": "synthetic (seeded FLUX-shaped tensors; FLUX.1-dev weights unavailable offline)",
+            "config": {"workload": wl.name, "M_per_gpu": M, "K": K, "N": N,
+                       "global_tokens": M * world, "x": "bf16", "out": "bf16",
+                       "parallelism": f"M-shard x{world}, weights replicated, no collective",
+                       "l2": "flushed between steps (256 MiB write)"},
+            "roofline": {"bound": "tensor", "kernel": "fp8_gemm_kernel",
+                         "achieved": round(gemm_tflops, 1), "peak": round(fp8_peak, 1),
+                         "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
+                         "traffic": traffic,
+                         "peak_basis": f"2 x {pk['source']} bf16 dense ({pk['bf16_tflops']} TFLOP/s)",
+                         "frac_of_nominal_4p5pf": round(gemm_tflops / NOMINAL_FP8_TFLOPS, 4),
+                         "gemm_us": round(g_ms * 1e3, 2)},
+            "quantizer": {"achieved": round(quant_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                          "frac": round(quant_gbs / pk["hbm_gbs"], 4),
+                          "us": round(q_ms * 1e3, 2), "bytes": wl.quant_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+                    "ms_per_step": round(e2e_total / args.steps, 4),
+                    "path": "C ABI fp8lin_fp8_linear with pinned host buffers"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+            "watchdog_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    from fp8linear_b200.workloads import WORKLOADS
+
+    wl = WORKLOADS[args.workload]
+    rows = args.cpu_rows
+    threads = os.cpu_count() or 1
+    st = cpu_reference_runner(wl, rows, threads=threads)
+    for _ in range(args.warmup):
+        st()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        st()
+        times.append(time.perf_counter() - t0)
+    per = sum(times) / len(times)
+    value = 2 * rows * wl.N * wl.K / per / 1e12
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 5),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3",
+        "data": "synthetic (seeded FLUX-shaped tensors)",
+        "config": {"workload": wl.name, "M_per_gpu": wl.M, "K": wl.K, "N": wl.N,
+                   "sample_rows": rows, "x": "bf16"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{rows} of {wl.M} token rows per step of {wl.name}; the "
+                                   "reference has no CPU kernels, so its path is the CPU "
+                                   "restatement (oracle port): per-token e4m3 quant, fp32 "
+                                   "matmul of decoded codes, dequant + bias"},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    gpu_ref = reference_gpu_timing(wl, args) if torch.cuda.is_available() else None
+    if gpu_ref is not None:
+        line["gpu_reference"] = gpu_ref
+    print(json.dumps(line), flush=True)
+
+
+def reference_gpu_timing(wl, args):
+    """Device time of the reference's own compiled CUDA ops (cuBLASLt FP8 GEMM + dequant
+    kernel, fp16 out, then the .to(bf16) cast Fp8Linear.forward applies), if built."""
+    try:
+        from oracle import build_ref
+        ref = build_ref.load()
+    except Exception as e:  # pragma: no cover
+        return {"unavailable": f"reference ops failed to load: {e}"}
+    if ref is None:
+        return {"unavailable": "oracle/_ref not built"}
+    from fp8linear_b200.workloads import make_weight, make_x
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    x = make_x(wl, gen_device="cuda")
+    w, b = make_weight(wl, gen_device="cuda")
+    wq, ws = ref.quantize_weight(w)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        ref.fp8_linear(x, wq, ws, b).to(x.dtype)
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ref.fp8_linear(x, wq, ws, b).to(x.dtype)
+        c.record(stream)
+        evs.append((a, c))
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(c) for a, c in evs)
+    return {"value": round(wl.flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4),
+            "what": "reference fp8_linear (quantize_fp8 + cuBLASLt FP8 GEMM into fp32 + "
+                    "dequant_bias_kernel, fp16 out) + .to(bf16), compiled from the "
+                    "reference sources for sm_100a"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="flux_qkv")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-rows", type=int, default=128)
+    ap.add_argument("--cpu-seconds", type=float, default=5.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)  # the timing rules ask for at least 3 warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -9,7 +9,8 @@ Two shared objects are produced next to this file:
 * ``_C.so`` -- the thin torch binding (TORCH_LIBRARY ``fp8linear_b200``) that
   calls the C ABI; loaded with ``torch.ops.load_library``.
 
-``python -m fp8linear_b200._build`` (or ``build()``) rebuilds what is stale.
+``python fp8linear_b200/_build.py`` (or ``build()``) rebuilds what is stale; it is a
+plain script so it runs before the package (whose import needs the binding) can load.
 """
 from __future__ import annotations
 
@@ -87,7 +88,11 @@ def build_binding(verbose: bool = False) -> Path:
     if not _stale(BINDING, deps):
         return BINDING
     inc, libdir, abi = _torch_paths()
-    cxx = shutil.which(os.environ.get("CXX", "g++")) or "g++"
+    # The system g++ links libstdc++ dynamically. A compiler that embeds a static
+    # libstdc++ in the binding breaks C++ exceptions thrown by torch (TORCH_CHECK)
+    # when they unwind through the binding's frames.
+    cxx = os.environ.get("FP8LIN_CXX") or ("/usr/bin/g++" if Path("/usr/bin/g++").exists()
+                                           else shutil.which("g++") or "g++")
     tmp = BINDING.with_name(BINDING.name + f".tmp{os.getpid()}")
     cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
            *[f"-isystem{p}" for p in inc], f"-isystem{CUDA_HOME / 'include'}",
@@ -96,6 +101,11 @@ def build_binding(verbose: bool = False) -> Path:
            "-ltorch_cpu", "-ltorch_cuda",
            f"-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{libdir}", f"-Wl,-rpath,{CUDA_HOME / 'lib64'}"]
     _run(cmd, verbose)
+    needed = subprocess.run(["readelf", "-d", str(tmp)], capture_output=True, text=True).stdout
+    if "libstdc++" not in needed:
+        os.unlink(tmp)
+        raise RuntimeError(f"{cxx} linked libstdc++ statically into the torch binding; "
+                           "set FP8LIN_CXX to a g++ that links it dynamically")
     os.replace(tmp, BINDING)
     return BINDING
 

@@ -21,7 +21,7 @@ def _load() -> None:
     if not _BINDING.exists():
         raise ImportError(
             f"fp8linear_b200 native binding not built ({_BINDING} missing); "
-            "run `python -m fp8linear_b200._build`"
+            "run `python fp8linear_b200/_build.py`"
         )
     try:
         torch.ops.load_library(str(_BINDING))

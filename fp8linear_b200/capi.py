@@ -37,7 +37,7 @@ class CApi:
     def __init__(self, path: str | Path = LIB_PATH):
         self.path = Path(path)
         if not self.path.exists():
-            raise ImportError(f"{self.path} not built; run `python -m fp8linear_b200._build`")
+            raise ImportError(f"{self.path} not built; run `python fp8linear_b200/_build.py`")
         self.lib = ctypes.CDLL(str(self.path))
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(self.lib, name)

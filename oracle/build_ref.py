@@ -14,7 +14,7 @@ Recipe (the reference's nix/kernel-builder build is not used):
   * ``TORCH_CUDA_ARCH_LIST=10.0a`` -> ``-gencode arch=compute_100a,code=sm_100a``
   * ``-U__CUDA_NO_HALF_CONVERSIONS__`` and friends, because ``fp8_gemm.cu:77``
     converts ``__half`` to ``float`` implicitly and torch's default flags forbid it
-  * link ``-lcublasLt -lcublas``
+  * link ``-lcublasLt -lcublas``; host compiler /usr/bin/g++ (shared libstdc++)
 The result is ``oracle/_ref/fp8linear_ref.so``; loading it with
 ``torch.ops.load_library`` registers the reference ops under ``torch.ops.fp8linear_ref``.
 
@@ -56,6 +56,10 @@ def build(verbose: bool = False) -> Path | None:
     if up_to_date():
         return SO_PATH
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    # A compiler wrapper that links libstdc++ statically breaks C++ exceptions that
+    # torch throws through the extension's frames; use the system g++.
+    if Path("/usr/bin/g++").exists():
+        os.environ["CXX"] = "/usr/bin/g++"
     os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 4))
     from torch.utils import cpp_extension
 
