@@ -30,7 +30,11 @@ SIGNATURES = {
     "fp8lin_linear_workspace_size": (_SZ, [_I64, _I64]),
     "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
     "fp8lin_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
+    "fp8lin_fp8_linear_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
 }
+
+# fp8lin_fp8_linear_noalloc's fixed scratch (FP8LIN_NOALLOC_SCRATCH_BYTES in the header)
+NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024
 
 
 class CApi:
@@ -106,6 +110,20 @@ class CApi:
             out.data_ptr(), DTYPE[out.dtype], M, N, K, workspace.data_ptr(),
             workspace.numel(), self._stream(x))
         self._check(rc, "fp8lin_fp8_linear")
+        return out
+
+    def fp8_linear_noalloc(self, x, wq, w_scale, bias=None, out=None):
+        """fp8_linear without a workspace: the library's fixed device scratch is used
+        (for callers that cannot allocate device memory)."""
+        M, K = x.shape
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device) if out is None else out
+        rc = self.lib.fp8lin_fp8_linear_noalloc(
+            x.data_ptr(), DTYPE[x.dtype], wq.data_ptr(), w_scale.data_ptr(),
+            None if bias is None else bias.data_ptr(),
+            DTYPE_NONE if bias is None else DTYPE[bias.dtype],
+            out.data_ptr(), DTYPE[out.dtype], M, N, K, self._stream(x))
+        self._check(rc, "fp8lin_fp8_linear_noalloc")
         return out
 
     def device_status(self, clear: bool = False) -> int:

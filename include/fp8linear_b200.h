@@ -124,6 +124,34 @@ FP8LIN_API int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq,
                                  void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Size of the device scratch array fp8lin_fp8_linear_noalloc works in (64 MiB).
+ * Every GPU that loads the library holds this array until the process exits.
+ */
+#define FP8LIN_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+
+/*
+ * fp8lin_fp8_linear for callers that cannot allocate device memory: no workspace
+ * argument; the activations' e4m3 codes and scales go to a fixed array of
+ * FP8LIN_NOALLOC_SCRATCH_BYTES inside the library instead. Meant for hosts that give
+ * an op only its input and output buffers (plugin/custom-op interfaces whose device
+ * memory is owned by the host's pool) or cannot afford cudaMalloc's implicit
+ * synchronisation. No counterpart in the reference (its fp8_linear allocates with
+ * torch::empty, csrc/fp8_gemm.cu:162-166).
+ *   Arguments, results and errors as fp8lin_fp8_linear, plus FP8LIN_ERR_WORKSPACE when
+ *   fp8lin_linear_workspace_size(M, K) > FP8LIN_NOALLOC_SCRATCH_BYTES.
+ *   All calls on a device share the one array: calls whose GPU work overlaps race on
+ *   it and must be serialised by the caller. It keeps the last call's contents;
+ *   nothing in it needs to start at zero.
+ *   The first call on each device looks up the array's device address
+ *   (cudaGetSymbolAddress, with that device current); make it before any stream
+ *   capture. No call allocates or frees device memory.
+ */
+FP8LIN_API int fp8lin_fp8_linear_noalloc(const void *x, int x_dtype, const void *wq,
+                                         const float *w_scale, const void *bias,
+                                         int bias_dtype, void *out, int out_dtype, int64_t M,
+                                         int64_t N, int64_t K, void *stream);
+
+/*
  * Watchdog status of the GEMM kernel on the current device: every wait in the
  * kernel is bounded; a wait that runs out sets a bit here and the kernel returns
  * early instead of hanging (1 = TMA producer, 2 = MMA issuer, 4 = epilogue).
