@@ -68,64 +68,110 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms in the background."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, polled through
+    NVML (the library nvidia-smi reads) every 2 ms on a background thread; falls back
+    to ``nvidia-smi -lms 200`` when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.rows: list[list[str]] = []
-        self.proc = None
+    def __init__(self, cuda_index: int, interval_s: float = 0.002):
+        self.cuda_index = cuda_index
+        self.interval = interval_s
+        self.samples: list[tuple[float, float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        self._proc = None
+        self._rows: list[list[str]] = []
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+            import pynvml as nv
+
+            nv.nvmlInit()
+            try:
+                idx = torch.cuda._get_nvml_device_index(self.cuda_index)
+            except Exception:
+                idx = self.cuda_index
+            h = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._nvml = nv
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                             nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                             int(reasons_fn(h))))
+                    except Exception:
+                        pass
+                    time.sleep(self.interval)
+
+            self._t = threading.Thread(target=poll, daemon=True)
+            self._t.start()
+        except Exception:
+            self._start_smi()
+        return self
+
+    def _start_smi(self):
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.cuda_index}", f"--query-gpu={fields}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
-            self.proc = None
-            return self
+            self._proc = None
+            return
 
         def pump():
-            for line in self.proc.stdout:
-                self.rows.append([c.strip() for c in line.split(",")])
+            for line in self._proc.stdout:
+                self._rows.append([c.strip() for c in line.split(",")])
 
         self._t = threading.Thread(target=pump, daemon=True)
         self._t.start()
-        return self
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
         if self._t:
             self._t.join(timeout=2)
-        sm, mx, reasons, power = [], [], set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-                power.append(float(r[3]))
-            except ValueError:
-                continue
-            for name, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "power_w_max": max(power) if power else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        sm, power, reasons = [], [], set()
+        if self._nvml is not None:
+            for mhz, w, bits in self.samples:
+                sm.append(mhz)
+                power.append(w)
+                for bit, name in self.REASONS.items():
+                    if bits & bit:
+                        reasons.add(name)
+            source = "nvml"
+        else:
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for r in self._rows:
+                try:
+                    sm.append(float(r[0]))
+                    self.max_mhz = float(r[1])
+                    power.append(float(r[2]))
+                except (ValueError, IndexError):
+                    continue
+                for name, v in zip(names, r[3:7]):
+                    if v.lower().startswith("active"):
+                        reasons.add(name)
+            source = "nvidia-smi"
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "power_w_max": max(power) if power else None, "samples": len(sm),
+                "reasons": sorted(reasons), "source": source}
 
 
 # ----------------------------------------------------------------------------- CPU path
@@ -207,14 +253,14 @@ def run_gpu(args):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---- warm-up
+    # ---- warm-up (the clock sampler starts here: the GPU is busy from now on)
+    clocks = ClockSampler(local).start()
     for _ in range(args.warmup):
         flush.zero_()
         step()
     barrier()
 
     # ---- timed: K fused steps, L2 flushed between steps
-    clocks = ClockSampler(local).start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     barrier()
@@ -224,7 +270,6 @@ def run_gpu(args):
         step()
         ev[i][1].record(stream)
     barrier()
-    clk = clocks.stop()
     step_ms = [a.elapsed_time(b_) for a, b_ in ev]
     total_ms = sum(step_ms)
     if world > 1:
@@ -295,6 +340,9 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_total = float(t.item())
     e2e_value = world * flops_rank * args.steps / (e2e_total * 1e-3) / 1e12
+    # clocks were sampled from the first warm-up step through the e2e phase: the whole
+    # stretch of continuous GPU work that contains the timed region
+    clk = clocks.stop()
 
     status = capi.device_status()
 
@@ -450,8 +498,8 @@ def reference_gpu_timing(wl, args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="flux_qkv")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=128)
