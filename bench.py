@@ -402,6 +402,85 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def measure_workload(name: str, steps: int, warmup: int) -> dict:
+    """Per-workload device times of the fused op, the GEMM alone and the quantizer
+    alone (CUDA events, L2 flushed before every timed launch)."""
+    import fp8linear_b200 as f
+    from fp8linear_b200.workloads import WORKLOADS, make_weight, make_x
+
+    wl = WORKLOADS[name]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    x = make_x(wl, gen_device="cuda")
+    w, b = make_weight(wl, gen_device="cuda")
+    wq, ws = f.quantize_weight(w)
+    del w
+    xq, xs = f.quantize_fp8(x)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(warmup):
+            flush.zero_()
+            fn()
+        evs = []
+        for _ in range(steps):
+            flush.zero_()
+            a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            c.record(stream)
+            evs.append((a, c))
+        torch.cuda.synchronize(dev)
+        return statistics.median(a.elapsed_time(c) for a, c in evs)
+
+    fused = timed(lambda: f.fp8_linear(x, wq, ws, b))
+    gemm = timed(lambda: f.fp8_gemm(xq, xs, wq, ws, b))
+    quant = timed(lambda: f.quantize_fp8(x))
+    pk = peaks()
+    # bandwidth-aware roofline for the GEMM: min(tensor peak, AI x HBM)
+    ai = wl.flops / wl.gemm_bytes
+    roof = min(2.0 * pk["bf16_tflops"], ai * pk["hbm_gbs"] / 1e3)
+    g_tf = wl.flops / (gemm * 1e-3) / 1e12
+    return {"workload": name, "M": wl.M, "K": wl.K, "N": wl.N,
+            "fused_us": round(fused * 1e3, 2),
+            "fused_tflops": round(wl.flops / (fused * 1e-3) / 1e12, 1),
+            "gemm_us": round(gemm * 1e3, 2), "gemm_tflops": round(g_tf, 1),
+            "gemm_roofline_tflops": round(roof, 1), "gemm_frac": round(g_tf / roof, 4),
+            "quant_us": round(quant * 1e3, 2),
+            "quant_gbs": round(wl.quant_bytes / (quant * 1e-3) / 1e9, 1),
+            "quant_frac": round(wl.quant_bytes / (quant * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+
+
+def reference_workload(name: str, steps: int, warmup: int) -> dict:
+    """Device time of the reference's own compiled ops on one workload."""
+    from fp8linear_b200.workloads import WORKLOADS
+
+    wl = WORKLOADS[name]
+
+    class A:  # the knobs reference_gpu_timing reads
+        pass
+
+    a = A()
+    a.steps, a.warmup = steps, warmup
+    r = reference_gpu_timing(wl, a)
+    if r and "ms_per_step" in r:
+        r = {"workload": name, "ref_fused_us": round(r["ms_per_step"] * 1e3, 2),
+             "ref_fused_tflops": r["value"]}
+    return r
+
+
+def run_sweep(args):
+    from fp8linear_b200.workloads import WORKLOADS
+
+    torch.cuda.set_device(0)
+    names = args.sweep.split(",") if args.sweep != "all" else list(WORKLOADS)
+    for n in names:
+        r = reference_workload(n, args.steps, args.warmup) if args.impl == "reference" \
+            else measure_workload(n, args.steps, args.warmup)
+        print(json.dumps(r), flush=True)
+        torch.cuda.empty_cache()
+
+
 # ----------------------------------------------------------------------------- reference arm
 
 
@@ -505,9 +584,14 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=128)
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", default="",
+                    help="'all' or comma-separated workloads: one JSON line of per-kernel "
+                         "device times per workload (not the driver's line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # the timing rules ask for at least 3 warm-up steps
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

@@ -7,7 +7,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/fp8linear_b200.h"
+#include "fp8linear_b200.h"
 #include "internal.h"
 
 namespace fp8lin {
@@ -76,14 +76,12 @@ int check_gemm_args(const void *xq, const float *xs, const void *wq, const float
     return fail(FP8LIN_ERR_UNSUPPORTED,
                 o + ": K must be a positive multiple of 16 for FP8 matmul, got " +
                     std::to_string(K));
-  if (N % 8 != 0)
-    return fail(FP8LIN_ERR_UNSUPPORTED,
-                o + ": N must be a multiple of 8 (16-byte output rows), got " + std::to_string(N));
   if (M == 0 || N == 0) return FP8LIN_OK;
   if (!xq || !xs || !wq || !ws || !out)
     return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": null pointer");
-  if (!aligned(xq, 16) || !aligned(wq, 16) || !aligned(out, 16))
-    return fail(FP8LIN_ERR_UNSUPPORTED, o + ": xq, wq and out must be 16-byte aligned");
+  if (!aligned(xq, 16) || !aligned(wq, 16))
+    return fail(FP8LIN_ERR_UNSUPPORTED, o + ": xq and wq must be 16-byte aligned");
+  if (!aligned(out, 2)) return fail(FP8LIN_ERR_UNSUPPORTED, o + ": out must be 2-byte aligned");
   return FP8LIN_OK;
 }
 
@@ -190,9 +188,12 @@ int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq, const float *w
 int fp8lin_device_status(unsigned int *status, int clear) {
   clear_error();
   if (!status) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "device_status: null pointer");
+  unsigned int q = 0;
   cudaError_t e = read_gemm_status(status, clear != 0);
+  if (e == cudaSuccess) e = read_quant_status(&q, clear != 0);
   if (e != cudaSuccess)
     return fail(FP8LIN_ERR_CUDA, std::string("device_status: ") + cudaGetErrorString(e));
+  *status |= q;
   return FP8LIN_OK;
 }
 

@@ -8,20 +8,30 @@
 //   out[m,n] = fma(acc[m,n] * x_scale[m], w_scale[n], bias[n])    -> bf16 (or fp16)
 //   acc[m,n] = sum_k e4m3(xq[m,k]) * e4m3(wq[n,k])                 (fp32, tensor cores)
 //
-// CTA = 6 warps, one CTA per SM, persistent over output tiles of BM x BN = 128 x 256:
-//   warp 0     TMA producer: A (xq) and B (wq) K-blocks of 128 bytes into a STAGES-deep
-//              shared-memory ring (128-byte swizzle), one mbarrier pair per stage.
-//   warp 1     MMA issuer: one thread issues tcgen05.mma.kind::f8f6f4 (M=128, N=256,
-//              K=32) into one of two TMEM accumulators (2 x 256 fp32 columns), and
-//              tcgen05.commit frees smem stages / publishes finished accumulators.
-//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from the warp's TMEM lane
-//              quarter, apply scales + bias, pack to bf16, stage in swizzled smem and
-//              TMA-store 32x32 boxes. Double-buffered TMEM lets the epilogue of tile i
-//              overlap the main loop of tile i+1.
-// Every mbarrier wait is bounded (see kWaitLimitNs); a wait that runs out records a bit
-// in g_gemm_status, tells the other roles to stop, drains its in-flight copies and the
-// CTA frees its TMEM and returns.
-// No TMA multicast is used anywhere.
+// Two shapes of the same kernel (template parameter CG = CTAs per MMA):
+//   CG = 1: one CTA per SM owns 128 x 256 output tiles (tcgen05.mma.cta_group::1,
+//           M=128 N=256 K=32); used when M <= 128.
+//   CG = 2: a cluster of two CTAs (one per SM) owns 256 x 256 tiles
+//           (tcgen05.mma.cta_group::2, M=256 N=256 K=32, issued by the leader CTA):
+//           each CTA loads its 128 rows of A and its 128 rows of B, so every SM
+//           streams 32 KB per 128-byte K-block instead of 48 KB. No TMA multicast.
+// Per CTA: 6 warps, persistent over tiles.
+//   warp 0     TMA producer: A/B K-blocks of 128 bytes into a shared-memory ring (128-byte
+//              swizzle); CG = 2 signals the leader's "full" barrier (cta_group::2 load).
+//   warp 1     MMA issuer (leader CTA): one thread issues the MMAs into one of two TMEM
+//              accumulators (2 x 256 fp32 columns) and commits stage/accumulator barriers
+//              (multicast to both CTAs of a pair).
+//   warps 2-5  epilogue: tcgen05.ld 64 columns at a time from the warp's TMEM lane
+//              quarter, apply scales + bias, pack to bf16, stage in 128-byte-swizzled
+//              smem and TMA-store 32 x 64 boxes (128-byte rows: half the store requests of
+//              64-byte rows, measured 6% faster). Double-buffered TMEM lets the epilogue of
+//              tile i overlap the main loop of tile i+1.
+// Tile order: consecutive tiles (run concurrently by the persistent CTAs) walk the output
+// N-fastest when M >= N, M-fastest otherwise, so the larger operand streams from HBM once
+// while the concurrent tiles share it through L2.
+// Every mbarrier wait is bounded (kWaitLimitNs); a wait that runs out records a bit in
+// g_gemm_status, tells the CTA's other roles to stop, drains in-flight copies and MMAs,
+// and the CTA frees its TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -41,39 +51,44 @@ __device__ unsigned int g_gemm_status;  // watchdog bits (1 producer, 2 mma, 4 e
 
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 128;  // rows of A per CTA
+constexpr int BN = 256;  // output columns per tile
 constexpr int BK = 128;  // bytes == e4m3 elements per K-block (one 128B swizzle row)
 constexpr int UMMA_K = 32;
-constexpr int STAGES = 4;
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
-constexpr int EPI_COLS = 32;
+constexpr int EPI_COLS = 64;                     // columns per output store box (128 B rows)
 constexpr int TMEM_COLS = 2 * BN;
-constexpr uint32_t A_STAGE = BM * BK;  // 16 KB
-constexpr uint32_t B_STAGE = BN * BK;  // 32 KB
-constexpr uint32_t EPI_BUF = 32 * EPI_COLS * 2;  // 2 KB: 32 rows x 32 cols x 2 B
+constexpr uint32_t A_STAGE = BM * BK;            // 16 KB
+constexpr uint32_t EPI_BUF = 32 * EPI_COLS * 2;  // 4 KB: 32 rows x 64 cols x 2 B
+constexpr uint32_t PAR_BYTES = 2 * BN * 4;       // per epilogue warp: w_scale + bias of a tile
+constexpr uint32_t RING_BYTES = 160 * 1024;      // operand ring (both shapes)
 
-constexpr uint32_t PAR_BYTES = 2 * BN * 4;        // per epilogue warp: w_scale + bias of a tile
+template <int CG>
+struct Cfg {
+  static constexpr int B_ROWS = BN / CG;                       // B rows this CTA loads
+  static constexpr uint32_t B_STAGE = B_ROWS * BK;             // 32 KB (CG 1) / 16 KB (CG 2)
+  static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
+  static constexpr int STAGES = RING_BYTES / STAGE;            // 3 / 5
+  static constexpr uint32_t TX_BYTES = CG * STAGE;             // bytes landing per stage
+  static constexpr int TILE_M = BM * CG;
+  static constexpr uint32_t OFF_A = 0;
+  static constexpr uint32_t OFF_B = OFF_A + STAGES * A_STAGE;
+  static constexpr uint32_t OFF_EPI = OFF_B + STAGES * B_STAGE;
+  static constexpr uint32_t OFF_PAR = OFF_EPI + EPI_WARPS * 2 * EPI_BUF;
+  static constexpr uint32_t OFF_BAR = OFF_PAR + EPI_WARPS * PAR_BYTES;
+  static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
+  static constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
+  static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
+  static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + base alignment slack
+  static constexpr uint32_t IDESC = ptx::idesc_e4m3_f32(TILE_M, BN);
+  static_assert(STAGES * STAGE <= RING_BYTES, "ring");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(OFF_B % 1024 == 0 && OFF_EPI % 1024 == 0, "swizzle atoms need 1024 B alignment");
+};
 
-constexpr uint32_t OFF_A = 0;
-constexpr uint32_t OFF_B = OFF_A + STAGES * A_STAGE;
-constexpr uint32_t OFF_EPI = OFF_B + STAGES * B_STAGE;
-constexpr uint32_t OFF_PAR = OFF_EPI + EPI_WARPS * 2 * EPI_BUF;
-constexpr uint32_t OFF_BAR = OFF_PAR + EPI_WARPS * PAR_BYTES;
-constexpr uint32_t NUM_BARS = 2 * STAGES + 5;  // full, empty, tmem full x2, tmem empty x2, drain
-constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
-constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
-constexpr uint32_t SMEM_USED = OFF_ABORT + 4;
-constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // slack to align the base to 1024 B
-
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-static_assert(OFF_B % 1024 == 0 && OFF_EPI % 1024 == 0, "swizzle atoms need 1024 B alignment");
-
-constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: far above any legitimate wait
+constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 1000000000ull;  // 1 s for in-flight copies on exit
-
-constexpr uint32_t IDESC = ptx::idesc_e4m3_f32(BM, BN);
 
 struct Params {
   const float *xs;
@@ -83,14 +98,20 @@ struct Params {
   int out_dtype;
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
+  int n_fastest;     // tile order
+  int direct_store;  // N % 8 != 0: rows are not 16-byte multiples, no TMA store
+  void *out;         // output base (direct stores)
   int pdl;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int &mt, int &nt) {
-  // M-fastest order: the CTAs running at the same time share one or two B tiles and
-  // stream the A tiles from L2.
-  mt = t % m_tiles;
-  nt = t / m_tiles;
+__device__ __forceinline__ void tile_coords(const Params &p, int t, int &mt, int &nt) {
+  if (p.n_fastest) {
+    mt = t / p.n_tiles;
+    nt = t - mt * p.n_tiles;
+  } else {
+    nt = t / p.m_tiles;
+    mt = t - nt * p.m_tiles;
+  }
 }
 
 __device__ __forceinline__ void record_timeout(unsigned bit, volatile int *abort) {
@@ -110,47 +131,54 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
   }
 }
 
+template <int CG>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_out, const Params p) {
+  using C = Cfg<CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = ptx::smem_u32(smem);
-  const uint32_t bar_full = sbase + OFF_BAR;             // STAGES barriers
-  const uint32_t bar_empty = bar_full + STAGES * 8;      // STAGES barriers
-  const uint32_t bar_tfull = bar_empty + STAGES * 8;     // 2 barriers
-  const uint32_t bar_tempty = bar_tfull + 2 * 8;         // 2 barriers
-  const uint32_t bar_drain = bar_tempty + 2 * 8;         // MMA drain on the way out
-  volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + OFF_TMEM_SLOT);
-  volatile int *abort = reinterpret_cast<volatile int *>(smem + OFF_ABORT);
+  const uint32_t bar_full = sbase + C::OFF_BAR;            // STAGES barriers
+  const uint32_t bar_empty = bar_full + C::STAGES * 8;     // STAGES barriers
+  const uint32_t bar_tfull = bar_empty + C::STAGES * 8;    // 2 barriers
+  const uint32_t bar_tempty = bar_tfull + 2 * 8;           // 2 barriers
+  const uint32_t bar_drain = bar_tempty + 2 * 8;           // MMA drain on the way out
+  volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + C::OFF_TMEM_SLOT);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + C::OFF_ABORT);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? ptx::cluster_ctarank() : 0u;  // 0 = leader (issues MMAs)
+  const bool leader = rank == 0;
+  const int group = blockIdx.x / CG;   // CTA pair (or single CTA) index
+  const int n_groups = gridDim.x / CG;
 
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
     ptx::prefetch_tmap(&tmap_out);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
       ptx::mbar_init(bar_empty + 8 * s, 1);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(bar_tfull + 8 * a, 1);
-      ptx::mbar_init(bar_tempty + 8 * a, EPI_WARPS);
+      ptx::mbar_init(bar_tempty + 8 * a, EPI_WARPS * CG);
     }
     ptx::mbar_init(bar_drain, 1);
     *abort = 0;
     ptx::fence_mbar_init();
   }
   if (warp == 1) {
-    ptx::tmem_alloc(sbase + OFF_TMEM_SLOT, TMEM_COLS);
-    ptx::tmem_relinquish();
+    ptx::tmem_alloc<CG>(sbase + C::OFF_TMEM_SLOT, TMEM_COLS);
+    ptx::tmem_relinquish<CG>();
   }
   ptx::tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) ptx::cluster_sync();  // peer barriers initialised before any signal
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -167,9 +195,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = group; t < num_tiles && ok; t += n_groups) {
         int mt, nt;
-        tile_coords(t, p.m_tiles, mt, nt);
+        tile_coords(p, t, mt, nt);
+        const int a_row = mt * C::TILE_M + static_cast<int>(rank) * BM;
+        const int b_row = nt * BN + static_cast<int>(rank) * C::B_ROWS;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!ptx::mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1u, abort, kWaitLimitNs)) {
             if (!*abort) record_timeout(1u, abort);
@@ -177,37 +207,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           const uint32_t fb = bar_full + 8 * stage;
-          ptx::mbar_arrive_expect_tx(fb, A_STAGE + B_STAGE);
-          ptx::tma_load_2d(sbase + OFF_A + stage * A_STAGE, &tmap_a, kb * BK, mt * BM, fb);
-          ptx::tma_load_2d(sbase + OFF_B + stage * B_STAGE, &tmap_b, kb * BK, nt * BN, fb);
+          const uint32_t dst_a = sbase + C::OFF_A + stage * A_STAGE;
+          const uint32_t dst_b = sbase + C::OFF_B + stage * C::B_STAGE;
+          if constexpr (CG == 1) {
+            ptx::mbar_arrive_expect_tx(fb, C::TX_BYTES);
+            ptx::tma_load_2d(dst_a, &tmap_a, kb * BK, a_row, fb);
+            ptx::tma_load_2d(dst_b, &tmap_b, kb * BK, b_row, fb);
+          } else {
+            // Both CTAs' bytes complete the leader's barrier; only the leader arms it.
+            if (leader) ptx::mbar_arrive_expect_tx(fb, C::TX_BYTES);
+            const uint32_t fb_leader = ptx::map_shared_rank(fb, 0);
+            ptx::tma_load_2d_pair(dst_a, &tmap_a, kb * BK, a_row, fb_leader);
+            ptx::tma_load_2d_pair(dst_b, &tmap_b, kb * BK, b_row, fb_leader);
+          }
           ++issued;
-          if (++stage == STAGES) {
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      // Drain: the last min(issued, STAGES) loads are the final use of their stages;
-      // wait (bounded) until their bytes have landed before the CTA can exit.
-      const uint32_t n_drain = issued < STAGES ? issued : STAGES;
+      // Drain: wait (bounded) until the MMAs have released the last min(issued, STAGES)
+      // stages, i.e. every load issued here has landed and been consumed.
+      const uint32_t n_drain = issued < C::STAGES ? issued : C::STAGES;
       for (uint32_t i = 0; i < n_drain; ++i) {
         if (stage == 0) {
-          stage = STAGES - 1;
+          stage = C::STAGES - 1;
           phase ^= 1u;
         } else {
           --stage;
         }
-        ptx::mbar_wait_timeout(bar_full + 8 * stage, phase, kDrainLimitNs);
+        ptx::mbar_wait_timeout(bar_empty + 8 * stage, phase, kDrainLimitNs);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = group; t < num_tiles && ok; t += n_groups, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!ptx::mbar_wait_bounded(bar_tempty + 8 * acc, acc_phase ^ 1u, abort, kWaitLimitNs)) {
@@ -223,45 +263,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           ptx::tc_fence_after();
-          const uint64_t adesc = ptx::sw128_kmajor_desc(sbase + OFF_A + stage * A_STAGE);
-          const uint64_t bdesc = ptx::sw128_kmajor_desc(sbase + OFF_B + stage * B_STAGE);
+          const uint64_t adesc = ptx::sw128_kmajor_desc(sbase + C::OFF_A + stage * A_STAGE);
+          const uint64_t bdesc = ptx::sw128_kmajor_desc(sbase + C::OFF_B + stage * C::B_STAGE);
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             // advance the start address by kk*32 bytes inside the swizzle atom
             const uint64_t koff = static_cast<uint64_t>((kk * UMMA_K) >> 4);
-            ptx::mma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, IDESC,
-                            (kb | kk) != 0 ? 1u : 0u);
+            const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
+            if constexpr (CG == 1)
+              ptx::mma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, C::IDESC, accumulate);
+            else
+              ptx::mma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, C::IDESC, accumulate);
           }
-          ptx::mma_commit(bar_empty + 8 * stage);  // stage reusable once these MMAs finish
-          if (++stage == STAGES) {
+          // the stage is reusable (in both CTAs) once these MMAs have read it
+          if constexpr (CG == 1)
+            ptx::mma_commit(bar_empty + 8 * stage);
+          else
+            ptx::mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        ptx::mma_commit(bar_tfull + 8 * acc);  // accumulator complete
+        // accumulator complete (both CTAs' halves)
+        if constexpr (CG == 1)
+          ptx::mma_commit(bar_tfull + 8 * acc);
+        else
+          ptx::mma_commit_pair_mc(bar_tfull + 8 * acc, 0x3);
       }
-      // No MMA may still be writing TMEM when the CTA frees it: commit everything
-      // issued so far to the drain barrier and wait (bounded) for it. On the normal
-      // path the last tile's MMAs are the only ones that can still be running.
-      ptx::mma_commit(bar_drain);
+      // No MMA may still be running when the CTAs free TMEM: commit everything issued
+      // so far to the drain barrier and wait (bounded) for it.
+      if constexpr (CG == 1)
+        ptx::mma_commit(bar_drain);
+      else
+        ptx::mma_commit_pair(bar_drain);
       ptx::mbar_wait_timeout(bar_drain, 0, kDrainLimitNs);
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int ew = warp - 2;
-    const uint32_t buf0 = sbase + OFF_EPI + static_cast<uint32_t>(ew) * 2 * EPI_BUF;
-    uint8_t *buf0_ptr = smem + OFF_EPI + ew * 2 * EPI_BUF;
-    float *par_ws = reinterpret_cast<float *>(smem + OFF_PAR + ew * PAR_BYTES);
+    const uint32_t buf0 = sbase + C::OFF_EPI + static_cast<uint32_t>(ew) * 2 * EPI_BUF;
+    uint8_t *buf0_ptr = smem + C::OFF_EPI + ew * 2 * EPI_BUF;
+    float *par_ws = reinterpret_cast<float *>(smem + C::OFF_PAR + ew * PAR_BYTES);
     float *par_b = par_ws + BN;
     uint32_t st_cnt = 0;
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int t = group; t < num_tiles; t += n_groups, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       int mt, nt;
-      tile_coords(t, p.m_tiles, mt, nt);
+      tile_coords(p, t, mt, nt);
       // Stage this tile's per-column w_scale and bias (as fp32) in the warp's own
       // smem slice while the main loop runs; columns past N read as 0.
       __syncwarp();
@@ -277,7 +330,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       ptx::tc_fence_after();
-      const int row0 = mt * BM + quarter * 32;
+      const int row0 = mt * C::TILE_M + static_cast<int>(rank) * BM + quarter * 32;
       const int row = row0 + lane;
       const float xs = row < p.M ? __ldg(p.xs + row) : 0.0f;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -287,10 +340,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c = 0; c < BN / EPI_COLS; ++c) {
         const int n0 = nt * BN + c * EPI_COLS;
         if (n0 >= p.N || !rows_live) break;  // warp-uniform
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS), r);
+        uint32_t r[64];
+        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS),
+                                *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS + 32),
+                                *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         ptx::tmem_wait_ld();
-        uint32_t packed[16];
+        uint32_t packed[32];
         const float4 *w4 = reinterpret_cast<const float4 *>(par_ws + c * EPI_COLS);
         const float4 *b4 = reinterpret_cast<const float4 *>(par_b + c * EPI_COLS);
 #pragma unroll
@@ -309,30 +365,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             packed[2 * j4 + 1] = ptx::pack_bf16x2(v2, v3);
           }
         }
-        // Reuse a staging buffer only after the store issued two boxes ago has read it.
-        if (lane == 0) ptx::bulk_wait_group_read<1>();
-        __syncwarp();
         const uint32_t b = st_cnt & 1u;
-        uint8_t *dst = buf0_ptr + b * EPI_BUF + lane * 64;
-        const int sw = (lane >> 1) & 3;  // 64-byte swizzle: 16B chunk ^= offset bits 7..8
+        if (!p.direct_store) {
+          // Reuse a staging buffer only after the store issued two boxes ago has read it.
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+          // row `lane` of the box: 8 16-byte chunks, 128-byte swizzle (chunk ^= row % 8)
+          uint8_t *dst = buf0_ptr + b * EPI_BUF + lane * 128;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 v =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          *reinterpret_cast<uint4 *>(dst + ((q ^ sw) << 4)) = v;
-        }
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ptx::tma_store_2d(&tmap_out, buf0 + b * EPI_BUF, n0, row0);
-          ptx::bulk_commit_group();
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4 *>(dst + ((q ^ (lane & 7)) << 4)) = make_uint4(
+                packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(&tmap_out, buf0 + b * EPI_BUF, n0, row0);
+            ptx::bulk_commit_group();
+          }
+        } else {
+          // Row pitch not a multiple of 16 bytes: transpose the 32 x 64 box through smem
+          // so that each store instruction writes 32 consecutive columns of one row.
+          uint8_t *box = buf0_ptr + b * EPI_BUF;
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4 *>(box + lane * 128 + q * 16) = make_uint4(
+                packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          __syncwarp();
+          const uint16_t *box16 = reinterpret_cast<const uint16_t *>(box);
+          uint16_t *out16 = reinterpret_cast<uint16_t *>(p.out);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int col = n0 + h * 32 + lane;
+            if (col < p.N) {
+              for (int r2 = 0; r2 < 32 && row0 + r2 < p.M; ++r2)
+                out16[static_cast<int64_t>(row0 + r2) * p.N + col] = box16[r2 * 64 + h * 32 + lane];
+            }
+          }
         }
         ++st_cnt;
       }
-      // All TMEM reads of this accumulator are complete (wait::ld above): release it.
+      // All TMEM reads of this accumulator are complete (wait::ld above): release it to
+      // the MMA issuer (the leader CTA's barrier for a pair).
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * acc);
+      if (lane == 0) {
+        if constexpr (CG == 1)
+          ptx::mbar_arrive(bar_tempty + 8 * acc);
+        else
+          ptx::mbar_arrive_cluster(ptx::map_shared_rank(bar_tempty + 8 * acc, 0));
+      }
     }
     if (lane == 0) ptx::bulk_wait_group<0>();
     __syncwarp();
@@ -341,9 +423,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncwarp();  // role loops ran on single lanes: reconverge before the CTA barrier
   ptx::tc_fence_before();
   __syncthreads();
+  // A pair stays resident until both CTAs are done: the leader's MMAs read the peer's
+  // shared memory and write its TMEM, and the peer arrives on the leader's barriers.
+  if constexpr (CG == 2) ptx::cluster_sync();
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+    ptx::tmem_dealloc<CG>(tmem_base, TMEM_COLS);
   }
 }
 
@@ -385,32 +470,64 @@ bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
   return true;
 }
 
-}  // namespace gemm
+// Per-device launch facts of one kernel shape: smem attribute set, co-resident groups.
+struct LaunchInfo {
+  bool ready = false;
+  cudaError_t err = cudaSuccess;
+  int max_groups = 0;
+};
 
-int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
-  using namespace gemm;
-  if (a.M == 0 || a.N == 0) return 0;
-  DeviceInfo dev;
-  if (!current_device_info(&dev)) return 5;
-  if (dev.cc_major != 10) {
-    set_error("fp8_gemm needs an sm_100 (B200-class) device; current device is sm_" +
-              std::to_string(dev.cc_major) + std::to_string(dev.cc_minor));
-    return 5;
+template <int CG>
+LaunchInfo &launch_info(int device, int sm_count) {
+  static LaunchInfo info[64];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  LaunchInfo &li = info[device & 63];
+  if (!li.ready) {
+    li.ready = true;
+    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(Cfg<CG>::SMEM_BYTES));
+    li.max_groups = sm_count / CG;
+    if (li.err == cudaSuccess && CG == 2) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(sm_count);
+      cfg.blockDim = dim3(NUM_THREADS);
+      cfg.dynamicSmemBytes = Cfg<CG>::SMEM_BYTES;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = CG;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG>, &cfg);
+      if (li.err == cudaSuccess) li.max_groups = std::min(li.max_groups, clusters);
+      if (li.err == cudaSuccess && li.max_groups < 1) li.err = cudaErrorInvalidConfiguration;
+    }
   }
-  if (a.M > 0x7fffffffLL || a.N > 0x7fffffffLL || a.K > 0x7fffffffLL) {
-    set_error("fp8_gemm: dimensions must fit in int32");
-    return 2;
-  }
+  return li;
+}
+
+template <int CG>
+int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
+  using C = Cfg<CG>;
   std::string err;
   CUtensorMap ta, tb, tout;
+  const bool direct = (a.N % 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) % 16) != 0;
   if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.xq, a.K, a.M, a.K, BK, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B, &err) ||
-      !make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wq, a.K, a.N, a.K, BK, BN,
+      !make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wq, a.K, a.N, a.K, BK, C::B_ROWS,
                     CU_TENSOR_MAP_SWIZZLE_128B, &err) ||
+      // rows of N bf16 are a 16-byte multiple only for N % 8 == 0: otherwise the
+      // epilogue stores directly and the (unused) output map is a placeholder over xq
       !make_tmap_2d(&tout,
                     a.out_dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                    a.out, a.N, a.M, a.N * 2, EPI_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B, &err)) {
+                    direct ? static_cast<const void *>(a.xq) : a.out, direct ? 8 : a.N, direct ? 1 : a.M, direct ? 16 : a.N * 2,
+                    direct ? 8 : EPI_COLS, direct ? 1 : 32, direct ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                                             : CU_TENSOR_MAP_SWIZZLE_128B,
+                    &err)) {
     set_error("fp8_gemm: " + err);
     return 4;
   }
@@ -423,44 +540,72 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   p.M = static_cast<int>(a.M);
   p.N = static_cast<int>(a.N);
   p.K = static_cast<int>(a.K);
-  p.m_tiles = static_cast<int>((a.M + BM - 1) / BM);
+  p.m_tiles = static_cast<int>((a.M + C::TILE_M - 1) / C::TILE_M);
   p.n_tiles = static_cast<int>((a.N + BN - 1) / BN);
   p.k_blocks = static_cast<int>((a.K + BK - 1) / BK);
+  p.n_fastest = a.M >= a.N ? 1 : 0;
+  p.direct_store = direct ? 1 : 0;
+  p.out = a.out;
   p.pdl = pdl ? 1 : 0;
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
   if (tiles > 0x7fffffffLL) {
     set_error("fp8_gemm: too many output tiles");
     return 2;
   }
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sm_count));
-
-  static std::once_flag attr_once[64];
-  cudaError_t ce = cudaSuccess;
-  std::call_once(attr_once[dev.device & 63], [&] {
-    ce = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(SMEM_BYTES));
-  });
-  if (ce != cudaSuccess) {
-    set_error(std::string("fp8_gemm: cudaFuncSetAttribute: ") + cudaGetErrorString(ce));
+  LaunchInfo &li = launch_info<CG>(dev.device, dev.sm_count);
+  if (li.err != cudaSuccess) {
+    set_error(std::string("fp8_gemm: kernel setup: ") + cudaGetErrorString(li.err));
     return 4;
   }
+  const int groups = static_cast<int>(std::min<int64_t>(tiles, li.max_groups));
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(groups * CG);
   cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (CG == 2) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = CG;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel, ta, tb, tout, p);
+  cfg.numAttrs = n;
+  cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG>, ta, tb, tout, p);
   if (ce != cudaSuccess) {
     set_error(std::string("fp8_gemm: launch failed: ") + cudaGetErrorString(ce));
     return 4;
   }
   return 0;
+}
+
+}  // namespace gemm
+
+int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
+  if (a.M == 0 || a.N == 0) return 0;
+  DeviceInfo dev;
+  if (!current_device_info(&dev)) return 5;
+  if (dev.cc_major != 10) {
+    set_error("fp8_gemm needs an sm_100 (B200-class) device; current device is sm_" +
+              std::to_string(dev.cc_major) + std::to_string(dev.cc_minor));
+    return 5;
+  }
+  if (a.M > 0x7fffffffLL || a.N > 0x7fffffffLL || a.K > 0x7fffffffLL) {
+    set_error("fp8_gemm: dimensions must fit in int32");
+    return 2;
+  }
+  // One 128-row tile per SM when M fits in it; CTA pairs with 256-row tiles otherwise.
+  if (a.M <= gemm::BM) return gemm::launch_shape<1>(a, dev, stream, pdl);
+  return gemm::launch_shape<2>(a, dev, stream, pdl);
 }
 
 cudaError_t read_gemm_status(unsigned int *bits, bool clear) {

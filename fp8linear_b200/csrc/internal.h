@@ -32,6 +32,8 @@ bool current_device_info(DeviceInfo *info);
 // Per-token quantization (activation path). Returns cudaSuccess or the launch error.
 cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
                                  float *scale, cudaStream_t stream, bool trigger_dependents);
+// Reads (and optionally clears) the quantizer watchdog bits (8) of the current device.
+cudaError_t read_quant_status(unsigned int *bits, bool clear);
 // Per-channel weight quantization (ATen semantics of the reference's quantize_weight).
 cudaError_t launch_quantize_weight(const void *w, int dtype, int64_t N, int64_t K, uint8_t *wq,
                                    float *scale, cudaStream_t stream);

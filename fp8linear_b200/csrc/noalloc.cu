@@ -26,7 +26,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/fp8linear_b200.h"
+#include "fp8linear_b200.h"
 #include "internal.h"
 
 namespace fp8lin {

@@ -21,10 +21,15 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "internal.h"
 #include "ptx.cuh"
 
 namespace fp8lin {
+
+__device__ unsigned int g_quant_status;  // watchdog bit 8: a quantizer wait ran out
+
 namespace {
 
 constexpr int kRowsBlock = 256;  // threads per CTA target for the vector kernel
@@ -92,6 +97,103 @@ __device__ __forceinline__ float quant_clamp(float x, float inv) {
   return fminf(fmaxf(v, -kE4M3Max), kE4M3Max);
 }
 
+// ---------------------------------------------------------------- fast row path
+//
+// Rows whose values are all finite (the normal case) take a cheaper path that gives the
+// same bits as the reference arithmetic:
+//  * amax: with the sign bits cleared, finite bf16/fp16 values order like their bit
+//    patterns read as unsigned integers, so a packed integer max (max.u16x2) over the
+//    magnitudes' bits, converted back exactly, equals fmaxf-reduce over |x|. The same
+//    max exposes a non-finite value in the row (bits above the largest finite pattern).
+//  * q = cvt_satfinite(x * inv): x and inv are finite, so no product is NaN, and the
+//    saturating convert maps anything beyond +-448 to +-448 exactly as the clamp
+//    fminf(fmaxf(v, -448), 448) before it would. x * inv uses packed IEEE multiplies.
+// Rows holding inf or NaN fall back to the literal clamp path (reference NaN/inf
+// semantics: NaN is ignored by the amax and clamps to -448; an inf amax gives inv = 0).
+template <typename T>
+struct Bits;
+template <>
+struct Bits<__nv_bfloat16> {
+  static constexpr uint32_t kMaxFinite = 0x7F7Fu;  // largest finite |bf16| pattern
+  __device__ __forceinline__ static float to_float(uint32_t b) { return __uint_as_float(b << 16); }
+};
+template <>
+struct Bits<__half> {
+  static constexpr uint32_t kMaxFinite = 0x7BFFu;  // largest finite |fp16| pattern
+  __device__ __forceinline__ static float to_float(uint32_t b) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+  }
+};
+
+// running max of the magnitude bit patterns of two packed 16-bit values
+__device__ __forceinline__ uint32_t mag_max2(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("{.reg .b32 t;\n\tand.b32 t, %2, 0x7fff7fff;\n\tmax.u16x2 %0, %1, t;}"
+      : "=r"(r)
+      : "r"(acc), "r"(w));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mag_max8(uint32_t acc, const uint4 &v) {
+  acc = mag_max2(acc, v.x);
+  acc = mag_max2(acc, v.y);
+  acc = mag_max2(acc, v.z);
+  return mag_max2(acc, v.w);
+}
+
+__device__ __forceinline__ uint32_t fold_halves(uint32_t acc) {
+  const uint32_t lo = acc & 0xFFFFu, hi = acc >> 16;
+  return lo > hi ? lo : hi;
+}
+
+// (a, b) * inv with one packed IEEE round-to-nearest multiply
+__device__ __forceinline__ void mul2(float &a, float &b, float inv) {
+  asm("{.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %4};\n\t"
+      "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;}"
+      : "=f"(a), "=f"(b)
+      : "f"(a), "f"(b), "f"(inv));
+}
+
+// 8 finite values -> 8 e4m3 codes (fast path)
+template <typename T>
+__device__ __forceinline__ uint2 quant8_fast(const uint4 &v, float inv) {
+  float f[8];
+  In<T>::unpack8(v, f);
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) mul2(f[i], f[i + 1], inv);
+  uint2 o;
+  o.x = static_cast<uint32_t>(ptx::cvt_e4m3x2(f[0], f[1])) |
+        (static_cast<uint32_t>(ptx::cvt_e4m3x2(f[2], f[3])) << 16);
+  o.y = static_cast<uint32_t>(ptx::cvt_e4m3x2(f[4], f[5])) |
+        (static_cast<uint32_t>(ptx::cvt_e4m3x2(f[6], f[7])) << 16);
+  return o;
+}
+
+// 8 values -> 8 e4m3 codes with the reference's literal clamp (any input)
+template <typename T>
+__device__ __forceinline__ uint2 quant8_clamp(const uint4 &v, float inv) {
+  float f[8];
+  In<T>::unpack8(v, f);
+  uint2 o;
+  o.x = static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[0], inv), quant_clamp(f[1], inv))) |
+        (static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[2], inv), quant_clamp(f[3], inv)))
+         << 16);
+  o.y = static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[4], inv), quant_clamp(f[5], inv))) |
+        (static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[6], inv), quant_clamp(f[7], inv)))
+         << 16);
+  return o;
+}
+
+// fmaxf-reduce of |x| over 8 values (NaN ignored), the slow-path amax
+template <typename T>
+__device__ __forceinline__ float amax8_float(float amax, const uint4 &v) {
+  float f[8];
+  In<T>::unpack8(v, f);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+  return amax;
+}
+
 // Vector kernel: TPR threads per row (multiple of 32), VPT 16-byte vectors per
 // thread, rows_per_cta = blockDim.x / TPR rows per CTA. Row r's vector j
 // (8 elements) is held by thread (j % TPR) as its (j / TPR)-th register vector.
@@ -102,7 +204,7 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const T *__restric
                                                               int64_t M, int K, int tpr,
                                                               int trigger) {
   if (trigger) ptx::grid_launch_dependents();
-  __shared__ float red[32];
+  __shared__ uint32_t red[32];
   const int t_in_row = threadIdx.x % tpr;
   const int row_in_cta = threadIdx.x / tpr;
   const int rows_per_cta = blockDim.x / tpr;
@@ -112,26 +214,53 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const T *__restric
   const T *xr = x + (row_ok ? row : 0) * static_cast<int64_t>(K);
 
   uint4 v[VPT];
-  float amax = 0.0f;
+  uint32_t mb = 0;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int j = t_in_row + i * tpr;
     if (row_ok && j < nvec) {
       v[i] = ld_stream_v4(xr + static_cast<int64_t>(j) * 8);
-      float f[8];
-      In<T>::unpack8(v[i], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+      mb = mag_max8(mb, v[i]);
     }
   }
-  amax = warp_max(amax);
+  mb = __reduce_max_sync(0xffffffffu, fold_halves(mb));
   const int warps_per_row = tpr >> 5;
+  bool finite;
   if (warps_per_row > 1) {
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    // Rows span several warps: exchange the per-warp maxima. The fast/slow decision is
+    // made for the whole CTA (any non-finite row -> every row takes the clamp path,
+    // which is exact for all rows), so the slow path's barriers stay CTA-uniform.
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mb;
     __syncthreads();
     const int base = row_in_cta * warps_per_row;
-    amax = red[base];
-    for (int w = 1; w < warps_per_row; ++w) amax = fmaxf(amax, red[base + w]);
+    uint32_t rmb = 0, any_nonfinite = 0;
+    for (int w = 0; w < warps_per_row; ++w) rmb = rmb > red[base + w] ? rmb : red[base + w];
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w)
+      any_nonfinite |= red[w] > Bits<T>::kMaxFinite ? 1u : 0u;
+    mb = rmb;
+    finite = any_nonfinite == 0;
+  } else {
+    finite = mb <= Bits<T>::kMaxFinite;  // warp == row: warp-uniform
+  }
+  float amax;
+  if (finite) {
+    amax = Bits<T>::to_float(mb);
+  } else {
+    amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int j = t_in_row + i * tpr;
+      if (row_ok && j < nvec) amax = amax8_float<T>(amax, v[i]);
+    }
+    amax = warp_max(amax);
+    if (warps_per_row > 1) {
+      __shared__ float redf[32];
+      if ((threadIdx.x & 31) == 0) redf[threadIdx.x >> 5] = amax;
+      __syncthreads();
+      const int base = row_in_cta * warps_per_row;
+      amax = redf[base];
+      for (int w = 1; w < warps_per_row; ++w) amax = fmaxf(amax, redf[base + w]);
+    }
   }
   if (!row_ok) return;
 
@@ -143,17 +272,123 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const T *__restric
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int j = t_in_row + i * tpr;
-    if (j < nvec) {
-      float f[8];
-      In<T>::unpack8(v[i], f);
-      uint2 o;
-      o.x = static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[0], inv), quant_clamp(f[1], inv))) |
-            (static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[2], inv), quant_clamp(f[3], inv)))
-             << 16);
-      o.y = static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[4], inv), quant_clamp(f[5], inv))) |
-            (static_cast<uint32_t>(ptx::cvt_e4m3x2(quant_clamp(f[6], inv), quant_clamp(f[7], inv)))
-             << 16);
-      *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) = o;
+    if (j < nvec)
+      *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) =
+          finite ? quant8_fast<T>(v[i], inv) : quant8_clamp<T>(v[i], inv);
+  }
+}
+
+// ---------------------------------------------------------------- streaming kernel
+//
+// Persistent: two CTAs per SM, each owning a contiguous block of rows. One producer
+// thread per CTA streams whole rows into a ring of row slots in shared memory with 1-D
+// bulk async copies (one cp.async.bulk per row, tracked by an mbarrier per slot), so an
+// SM keeps up to ~200 KB of x in flight with almost no registers. Up to 8 consumer
+// warps per CTA take one row each: amax over the row in shared memory, then the conversion
+// (same arithmetic as above) with coalesced 8-byte stores, then the slot is released.
+// Row j lives in slot j % nslot and is consumed by warp j % nwarps, with nwarps dividing
+// nslot: every use of a slot is consumed by the same warp, in order, so a warp never
+// waits on a later phase of a slot while an earlier phase of the same parity is live.
+constexpr int kBulkWarps = 8;
+constexpr int kBulkThreads = 32 * (kBulkWarps + 1);  // + the producer warp
+constexpr uint32_t kBulkRing = 100 * 1024;  // per CTA; two CTAs per SM
+constexpr int kBulkCtasPerSm = 2;
+// Inputs below this size stream better through the register kernel (one short wave).
+constexpr int64_t kBulkMinBytes = 48ll << 20;
+constexpr int kBulkMaxSlots = 64;
+constexpr uint64_t kQuantWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+
+template <typename T>
+__global__ void __launch_bounds__(kBulkThreads, 1)
+    quant_rows_bulk_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
+                           float *__restrict__ scale, int64_t M, int K, int nslot, int nwarps,
+                           int trigger) {
+  if (trigger) ptx::grid_launch_dependents();
+  extern __shared__ __align__(128) uint8_t qsm[];
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;
+  const uint32_t sbase = ptx::smem_u32(qsm);
+  const uint32_t bar_full = sbase + static_cast<uint32_t>(nslot) * row_bytes;  // 16B aligned
+  const uint32_t bar_empty = bar_full + 8u * static_cast<uint32_t>(nslot);
+  volatile int *abort = reinterpret_cast<volatile int *>(qsm + (bar_empty - sbase) + 8 * nslot);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int64_t per_cta = (M + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * per_cta;
+  const int64_t r1 = r0 + per_cta < M ? r0 + per_cta : M;
+  const int n = r1 > r0 ? static_cast<int>(r1 - r0) : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nslot; ++i) {
+      ptx::mbar_init(bar_full + 8 * i, 1);
+      ptx::mbar_init(bar_empty + 8 * i, 1);
+    }
+    *abort = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kBulkWarps) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int s = j % nslot;
+        const uint32_t ph = static_cast<uint32_t>(j / nslot) & 1u;
+        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kQuantWaitNs)) {
+          if (!*abort) {
+            atomicOr(&g_quant_status, 8u);
+            *abort = 1;
+          }
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(bar_full + 8 * s, row_bytes);
+        ptx::bulk_load_1d(sbase + static_cast<uint32_t>(s) * row_bytes,
+                          x + (r0 + j) * static_cast<int64_t>(K), row_bytes, bar_full + 8 * s);
+        ++issued;
+      }
+      // Drain: every issued row has been consumed (or the bounded wait gave up).
+      for (int j = issued - 1; j >= 0 && j >= issued - nslot; --j)
+        ptx::mbar_wait_timeout(bar_empty + 8 * (j % nslot),
+                               static_cast<uint32_t>(j / nslot) & 1u, kQuantWaitNs);
+    }
+  } else {
+    // ---------------------------------------------------------------- consumers
+    const int nchunk = K >> 3;  // 16-byte chunks (8 elements) per row
+    for (int j = warp; j < n && warp < nwarps; j += nwarps) {
+      const int s = j % nslot;
+      const uint32_t ph = static_cast<uint32_t>(j / nslot) & 1u;
+      if (!ptx::mbar_wait_bounded(bar_full + 8 * s, ph, abort, kQuantWaitNs)) {
+        if (lane == 0 && !*abort) {
+          atomicOr(&g_quant_status, 8u);
+          *abort = 1;
+        }
+        break;
+      }
+      const uint4 *row = reinterpret_cast<const uint4 *>(qsm + static_cast<uint32_t>(s) * row_bytes);
+      uint32_t mb = 0;
+      for (int c = lane; c < nchunk; c += 32) mb = mag_max8(mb, row[c]);
+      mb = __reduce_max_sync(0xffffffffu, fold_halves(mb));
+      const bool finite = mb <= Bits<T>::kMaxFinite;  // warp-uniform
+      float amax;
+      if (finite) {
+        amax = Bits<T>::to_float(mb);
+      } else {
+        amax = 0.0f;
+        for (int c = lane; c < nchunk; c += 32) amax = amax8_float<T>(amax, row[c]);
+        amax = warp_max(amax);
+      }
+      const float sc = fmaxf(__fdiv_rn(amax, kE4M3Max), kScaleFloor);
+      const float inv = __fdiv_rn(1.0f, sc);
+      const int64_t grow = r0 + j;
+      if (lane == 0) scale[grow] = sc;
+      uint2 *qrow = reinterpret_cast<uint2 *>(xq + grow * static_cast<int64_t>(K));
+      if (finite) {
+        for (int c = lane; c < nchunk; c += 32) qrow[c] = quant8_fast<T>(row[c], inv);
+      } else {
+        for (int c = lane; c < nchunk; c += 32) qrow[c] = quant8_clamp<T>(row[c], inv);
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);  // slot reusable
     }
   }
 }
@@ -240,12 +475,46 @@ __global__ void __launch_bounds__(256) quant_weight_kernel(const T *__restrict__
 }
 
 template <typename T>
+cudaError_t launch_rows_bulk(const T *xp, int64_t M, int64_t K, uint8_t *xq, float *scale,
+                             cudaStream_t stream, bool trigger, const DeviceInfo &dev) {
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;
+  const int64_t max_ctas = static_cast<int64_t>(kBulkCtasPerSm) * dev.sm_count;
+  const int64_t grid = M < max_ctas ? M : max_ctas;
+  const int64_t per_cta = (M + grid - 1) / grid;
+  int64_t nslot = kBulkRing / row_bytes;
+  if (nslot > kBulkMaxSlots) nslot = kBulkMaxSlots;
+  if (nslot > per_cta) nslot = per_cta;
+  // consumer warps: at most kBulkWarps and a divisor of the slot count (slot ownership)
+  const int64_t nwarps = nslot < kBulkWarps ? nslot : kBulkWarps;
+  nslot -= nslot % nwarps;
+  // slots + a full and an empty barrier per slot + the abort word
+  const size_t smem = static_cast<size_t>(nslot) * row_bytes + 16 * static_cast<size_t>(nslot) + 16;
+  static std::once_flag once[64];
+  cudaError_t e = cudaSuccess;
+  std::call_once(once[dev.device & 63], [&] {
+    e = cudaFuncSetAttribute(quant_rows_bulk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kBulkRing + 16 * kBulkMaxSlots + 16));
+  });
+  if (e != cudaSuccess) return e;
+  quant_rows_bulk_kernel<T><<<static_cast<unsigned>(grid), kBulkThreads, smem, stream>>>(
+      xp, xq, scale, M, static_cast<int>(K), static_cast<int>(nslot), static_cast<int>(nwarps),
+      trigger ? 1 : 0);
+  return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t launch_rows_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, float *scale,
                               cudaStream_t stream, bool trigger) {
   const T *xp = reinterpret_cast<const T *>(x);
   const int64_t nvec = K / 8;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(xq) % 8 == 0);
+  DeviceInfo dev;
+  // Streaming kernel for large inputs whose rows are whole multiples of 16 bytes and
+  // fit the ring twice; the register kernel below for the rest.
+  if (K % 8 == 0 && aligned && 2 * K * 2 <= static_cast<int64_t>(kBulkRing) &&
+      M * K * 2 >= kBulkMinBytes && current_device_info(&dev))
+    return launch_rows_bulk<T>(xp, M, K, xq, scale, stream, trigger, dev);
   int vpt = nvec >= 256 ? 8 : nvec >= 128 ? 4 : nvec >= 64 ? 2 : 1;
   int64_t tpr = ((nvec + vpt - 1) / vpt + 31) / 32 * 32;
   if (K % 8 == 0 && aligned && tpr <= 1024) {
@@ -277,6 +546,16 @@ cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K,
   if (dtype == kBF16)
     return launch_rows_typed<__nv_bfloat16>(x, M, K, xq, scale, stream, trigger_dependents);
   return launch_rows_typed<__half>(x, M, K, xq, scale, stream, trigger_dependents);
+}
+
+cudaError_t read_quant_status(unsigned int *bits, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(bits, g_quant_status, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_quant_status, &zero, sizeof(unsigned int));
+  }
+  return e;
 }
 
 cudaError_t launch_quantize_weight(const void *w, int dtype, int64_t N, int64_t K, uint8_t *wq,

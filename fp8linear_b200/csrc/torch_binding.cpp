@@ -19,7 +19,7 @@
 #include <torch/library.h>
 #include <torch/torch.h>
 
-#include "../../include/fp8linear_b200.h"
+#include "fp8linear_b200.h"
 
 namespace {
 
@@ -118,7 +118,6 @@ at::Tensor gemm_impl(const at::Tensor &xq, const at::Tensor &x_scale, const at::
   auto wqc = aligned16(wq);
   const int64_t M = xqc.size(0), K = xqc.size(1), N = wqc.size(0);
   TORCH_CHECK(K % 16 == 0, "K must be a multiple of 16 for FP8 matmul, got ", K);
-  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8 (16-byte bf16 output rows), got ", N);
   auto xs = x_scale.contiguous();
   auto ws = w_scale.contiguous();
   TORCH_CHECK(xs.scalar_type() == at::kFloat && ws.scalar_type() == at::kFloat,
@@ -163,7 +162,6 @@ at::Tensor fp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scale,
   auto wqc = aligned16(wq);
   const int64_t M = x2d.size(0), N = wqc.size(0);
   TORCH_CHECK(K % 16 == 0, "K must be a multiple of 16 for FP8 matmul, got ", K);
-  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8 (16-byte output rows), got ", N);
   auto ws = w_scale.contiguous();
   TORCH_CHECK(ws.numel() == N, "w_scale must have N entries (per-channel)");
   auto out_shape = x.sizes().vec();

@@ -93,8 +93,10 @@ FP8LIN_API int fp8lin_quantize_weight(const void *w, int w_dtype, int64_t N, int
  *   x_scale [M] fp32; w_scale [N] fp32
  *   bias [N] of bias_dtype (BF16/F16/F32) or NULL with FP8LIN_DTYPE_NONE
  *   out [M,N] row-major, out_dtype BF16 or F16 (the reference always writes fp16)
- * Requirements (checked): K % 16 == 0 and K > 0 (as csrc/fp8_gemm.cu:154), N % 8 == 0,
- * xq/wq/out 16-byte aligned. M == 0 or N == 0 is a no-op.
+ * Requirements (checked): K % 16 == 0 and K > 0 (as csrc/fp8_gemm.cu:154), xq/wq
+ * 16-byte aligned. Any N: output rows that are a multiple of 16 bytes (N % 8 == 0, out
+ * 16-byte aligned) are written with TMA stores, others with plain stores.
+ * M == 0 or N == 0 is a no-op.
  */
 FP8LIN_API int fp8lin_fp8_gemm(const void *xq, const float *x_scale, const void *wq,
                                const float *w_scale, const void *bias, int bias_dtype,
@@ -152,9 +154,9 @@ FP8LIN_API int fp8lin_fp8_linear_noalloc(const void *x, int x_dtype, const void 
                                          int64_t N, int64_t K, void *stream);
 
 /*
- * Watchdog status of the GEMM kernel on the current device: every wait in the
- * kernel is bounded; a wait that runs out sets a bit here and the kernel returns
- * early instead of hanging (1 = TMA producer, 2 = MMA issuer, 4 = epilogue).
+ * Watchdog status of the kernels on the current device: every wait in them is
+ * bounded; a wait that runs out sets a bit here and the kernel returns early instead
+ * of hanging (GEMM: 1 = TMA producer, 2 = MMA issuer, 4 = epilogue; 8 = quantizer).
  * *status receives the bits; clear != 0 resets them. Synchronous on the device.
  * No counterpart in the reference (cuBLASLt has no such report).
  */

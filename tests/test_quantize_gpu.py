@@ -135,3 +135,42 @@ def test_quantize_capi_matches_op(capi):
     b = capi.quantize_fp8(x)
     assert torch.equal(a[0].view(torch.uint8), b[0].view(torch.uint8))
     assert torch.equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("M,K", [(2000, 15360), (1500, 10240), (3000, 7168), (700, 40960),
+                                 (5000, 3072), (149, 12288), (4608, 12296), (8192, 3072),
+                                 (3000, 12288), (4000, 10240), (20000, 1024)])
+def test_quantize_ring_configs(M, K):
+    """Inputs large enough for the streaming kernel, at widths where its shared-memory row
+    ring holds 3, 4, 5, 8 or 16 rows, plus register-kernel sizes: every row still
+    quantizes bit-exactly."""
+    from fp8linear_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    x = (torch.randn(M, K, device="cuda", generator=g) *
+         torch.logspace(-2, 2, M, device="cuda")[:, None]).bfloat16()
+    xq, xs = ops.quantize_fp8(x)
+    tq, ts = torch_quant_ref(x)
+    assert torch.equal(xq.view(torch.uint8), tq.view(torch.uint8))
+    assert torch.equal(xs.view(torch.int32), ts.view(torch.int32))
+
+
+@pytest.mark.parametrize("K", [3072, 12288, 15360])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_quantize_nonfinite_rows_wide(K, dtype, oracle):
+    """Rows with inf/NaN next to finite rows at FLUX widths: the rows spanning several
+    warps exercise the CTA-wide fallback to the clamp path."""
+    from fp8linear_b200 import ops
+
+    M = 300
+    g = torch.Generator().manual_seed(K)
+    x = torch.randn(M, K, generator=g) * 3
+    for r in range(0, M, 37):
+        x[r, (r * 7) % K] = float("nan")
+    for r in range(5, M, 53):
+        x[r, (r * 3) % K] = float("inf") if r % 2 else -float("inf")
+    x = x.to(dtype)
+    xq, xs = ops.quantize_fp8(x.cuda())
+    oq, osc = oracle.c_quantize_rows(bits16(x), 0 if dtype == torch.bfloat16 else 1)
+    assert np.array_equal(codes(xq), oq)
+    assert np.array_equal(u32(xs), osc.view(np.uint32))
