@@ -504,6 +504,13 @@ def run_nshard(args):
     wqs, wss, bs = S.shard_columns(wq, ws, b, world, rank)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    fused = None
+    if args.fused:
+        from fp8linear_b200.capi import CApi
+
+        capi = CApi()
+        fused = S.FusedColumnParallel(wl.M, wl.N, torch.bfloat16, dev) if world > 1 else None
+        work = torch.empty(capi.workspace_size(wl.M, wl.K), dtype=torch.uint8, device=dev)
 
     def barrier():
         if world > 1:
@@ -511,6 +518,13 @@ def run_nshard(args):
         torch.cuda.synchronize(dev)
 
     def step(timing=None):
+        if fused is not None:
+            # one kernel pair: the epilogue writes every rank's buffer; the GEMM and the
+            # NVLink transfer are one, so there is no separate compute/gather split
+            out = fused(x, wqs, wss, bs, capi, workspace=work)
+            if timing is not None:
+                timing.record(stream)
+            return out
         local = f.fp8_linear(x, wqs, wss, bs)
         if timing is not None:
             timing.record(stream)
@@ -547,10 +561,12 @@ def run_nshard(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "e4m3",
             "data": "synthetic (seeded FLUX-shaped tensors)",
             "config": {"workload": wl.name, "M": wl.M, "K": wl.K, "N": wl.N,
-                       "parallelism": f"N-shard x{world} (column parallel) + NCCL all-gather",
+                       "parallelism": f"N-shard x{world} (column parallel) + " + (
+                           "all-gather fused into the GEMM epilogue (NVLink P2P stores)"
+                           if args.fused else "NCCL all-gather"),
                        "l2": "flushed between steps (256 MiB write)"},
-            "compute_ms_per_step": round(comp / args.steps, 5),
-            "allgather_ms_per_step": round((total - comp) / args.steps, 5),
+            "compute_ms_per_step": None if args.fused else round(comp / args.steps, 5),
+            "allgather_ms_per_step": None if args.fused else round((total - comp) / args.steps, 5),
             "allgather_bytes_per_rank": gather_bytes,
             "gpu_launches": 2 * args.steps, "clocks": clk}), flush=True)
     if world > 1:
@@ -664,6 +680,8 @@ def main():
     ap.add_argument("--mode", choices=["mshard", "nshard"], default="mshard",
                     help="multi-GPU split: token rows (default, no collective) or output "
                          "channels with an NCCL all-gather")
+    ap.add_argument("--fused", action="store_true",
+                    help="with --mode nshard: fuse the all-gather into the GEMM epilogue")
     ap.add_argument("--sweep", default="",
                     help="'all' or comma-separated workloads: one JSON line of per-kernel "
                          "device times per workload (not the driver's line)")

@@ -31,6 +31,8 @@ SIGNATURES = {
     "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
     "fp8lin_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
     "fp8lin_fp8_linear_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
+    "fp8lin_fp8_linear_allgather": (_I, [_P, _I, _P, _P, _P, _I, ctypes.POINTER(ctypes.c_void_p),
+                                         _I, _I, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
 }
 
 # fp8lin_fp8_linear_noalloc's fixed scratch (FP8LIN_NOALLOC_SCRATCH_BYTES in the header)
@@ -125,6 +127,26 @@ class CApi:
             out.data_ptr(), DTYPE[out.dtype], M, N, K, self._stream(x))
         self._check(rc, "fp8lin_fp8_linear_noalloc")
         return out
+
+    def fp8_linear_allgather(self, x, wq, w_scale, bias, out_ptrs, ldo, out_dtype=None,
+                             workspace=None):
+        """Column-parallel linear writing this rank's [M, N] block (N = wq rows) into
+        every buffer in ``out_ptrs`` (device addresses of this rank's first column in each
+        GPU's [M, ldo] output; the first is this GPU's)."""
+        M, K = x.shape
+        N = wq.shape[0]
+        out_dtype = x.dtype if out_dtype is None else out_dtype
+        need = self.workspace_size(M, K)
+        if workspace is None:
+            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=x.device)
+        arr = (ctypes.c_void_p * len(out_ptrs))(*[int(p) for p in out_ptrs])
+        rc = self.lib.fp8lin_fp8_linear_allgather(
+            x.data_ptr(), DTYPE[x.dtype], wq.data_ptr(), w_scale.data_ptr(),
+            None if bias is None else bias.data_ptr(),
+            DTYPE_NONE if bias is None else DTYPE[bias.dtype],
+            arr, len(out_ptrs), DTYPE[out_dtype], M, N, K, ldo, workspace.data_ptr(),
+            workspace.numel(), self._stream(x))
+        self._check(rc, "fp8lin_fp8_linear_allgather")
 
     def device_status(self, clear: bool = False) -> int:
         v = ctypes.c_uint(0)

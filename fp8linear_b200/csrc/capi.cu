@@ -185,6 +185,47 @@ int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq, const float *w
   return launch_gemm(a, s, true);
 }
 
+int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, const float *w_scale,
+                                const void *bias, int bias_dtype, void *const *outs, int n_outs,
+                                int out_dtype, int64_t M, int64_t N, int64_t K, int64_t ldo,
+                                void *workspace, size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear_allgather: x must be fp16 or bf16");
+  if (!outs || n_outs < 1 || n_outs > 1 + kMaxPeers)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear_allgather: n_outs must be 1..8");
+  if (ldo < N) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear_allgather: ldo < N");
+  int rc = check_gemm_args(reinterpret_cast<const void *>(16), w_scale, wq, w_scale, bias,
+                           bias_dtype, outs[0], out_dtype, M, N, K, "fp8_linear_allgather");
+  if (rc != FP8LIN_OK || M == 0 || N == 0) return rc;
+  if (N % 8 != 0 || ldo % 8 != 0)
+    return fail(FP8LIN_ERR_UNSUPPORTED, "fp8_linear_allgather: N and ldo must be multiples of 8");
+  for (int i = 0; i < n_outs; ++i)
+    if (!outs[i] || !aligned(outs[i], 16))
+      return fail(FP8LIN_ERR_UNSUPPORTED,
+                  "fp8_linear_allgather: every output pointer must be 16-byte aligned");
+  if (!x) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear_allgather: null x");
+  const size_t need = fp8lin_linear_workspace_size(M, K);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, kWsAlign))
+    return fail(FP8LIN_ERR_WORKSPACE, "fp8_linear_allgather: workspace of " +
+                                          std::to_string(need) +
+                                          " bytes (256-byte aligned) required");
+  uint8_t *xq = static_cast<uint8_t *>(workspace);
+  float *xs = reinterpret_cast<float *>(
+      xq + round_up(static_cast<size_t>(M) * static_cast<size_t>(K), kWsAlign));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_quantize_rows(x, x_dtype, M, K, xq, xs, s, true);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("fp8_linear_allgather: quantize launch: ") +
+                                     cudaGetErrorString(e));
+  GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
+             bias ? bias_dtype : kNone, outs[0], out_dtype, M, N, K};
+  a.ldo = ldo;
+  a.n_peers = n_outs - 1;
+  a.peers = outs + 1;
+  return launch_gemm(a, s, true);
+}
+
 int fp8lin_device_status(unsigned int *status, int clear) {
   clear_error();
   if (!status) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "device_status: null pointer");

@@ -99,8 +99,11 @@ struct Params {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
   int n_fastest;     // tile order
-  int direct_store;  // N % 8 != 0: rows are not 16-byte multiples, no TMA store
+  int direct_store;  // rows not 16-byte multiples / unaligned: no TMA store
   void *out;         // output base (direct stores)
+  int ldo;           // output row pitch (elements)
+  int n_peers;       // peer copies of every output box (P2P stores)
+  void *peers[kMaxPeers];
   int pdl;
 };
 
@@ -382,6 +385,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ptx::tma_store_2d(&tmap_out, buf0 + b * EPI_BUF, n0, row0);
             ptx::bulk_commit_group();
           }
+          if (p.n_peers > 0) {
+            // Same box to every peer GPU's buffer over NVLink: re-read it coalesced
+            // (lane -> row 4i + lane/8, 16-byte chunk lane%8), one full 128-byte line
+            // per 8 lanes per store instruction. Plain P2P stores; no TMA to peers.
+            const int pr = lane >> 3, pc = lane & 7;
+            const uint8_t *box = buf0_ptr + b * EPI_BUF;
+            uint4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int rr = 4 * i + pr;
+              v[i] = *reinterpret_cast<const uint4 *>(box + rr * 128 + ((pc ^ (rr & 7)) << 4));
+            }
+            const bool col_ok = n0 + pc * 8 < p.N;
+            for (int q = 0; q < p.n_peers; ++q) {
+              uint16_t *dst = reinterpret_cast<uint16_t *>(p.peers[q]);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int rr = row0 + 4 * i + pr;
+                if (col_ok && rr < p.M)
+                  *reinterpret_cast<uint4 *>(dst + static_cast<int64_t>(rr) * p.ldo + n0 + pc * 8) =
+                      v[i];
+              }
+            }
+            __syncwarp();
+          }
         } else {
           // Row pitch not a multiple of 16 bytes: transpose the 32 x 64 box through smem
           // so that each store instruction writes 32 consecutive columns of one row.
@@ -399,7 +427,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int col = n0 + h * 32 + lane;
             if (col < p.N) {
               for (int r2 = 0; r2 < 32 && row0 + r2 < p.M; ++r2)
-                out16[static_cast<int64_t>(row0 + r2) * p.N + col] = box16[r2 * 64 + h * 32 + lane];
+                out16[static_cast<int64_t>(row0 + r2) * p.ldo + col] = box16[r2 * 64 + h * 32 + lane];
             }
           }
         }
@@ -417,6 +445,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (lane == 0) ptx::bulk_wait_group<0>();
+    // Peer copies are plain stores to other GPUs' memory: make them visible system-wide
+    // before this kernel's completion is signalled to anything that reads them.
+    if (p.n_peers > 0) __threadfence_system();
     __syncwarp();
   }
 
@@ -514,7 +545,9 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   using C = Cfg<CG>;
   std::string err;
   CUtensorMap ta, tb, tout;
-  const bool direct = (a.N % 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) % 16) != 0;
+  const int64_t ldo = a.ldo > 0 ? a.ldo : a.N;
+  const bool direct = (a.N % 8) != 0 || (ldo % 8) != 0 ||
+                      (reinterpret_cast<uintptr_t>(a.out) % 16) != 0;
   if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.xq, a.K, a.M, a.K, BK, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B, &err) ||
       !make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wq, a.K, a.N, a.K, BK, C::B_ROWS,
@@ -524,7 +557,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
       !make_tmap_2d(&tout,
                     a.out_dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                    direct ? static_cast<const void *>(a.xq) : a.out, direct ? 8 : a.N, direct ? 1 : a.M, direct ? 16 : a.N * 2,
+                    direct ? static_cast<const void *>(a.xq) : a.out, direct ? 8 : a.N, direct ? 1 : a.M, direct ? 16 : ldo * 2,
                     direct ? 8 : EPI_COLS, direct ? 1 : 32, direct ? CU_TENSOR_MAP_SWIZZLE_NONE
                                                              : CU_TENSOR_MAP_SWIZZLE_128B,
                     &err)) {
@@ -546,6 +579,14 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   p.n_fastest = a.M >= a.N ? 1 : 0;
   p.direct_store = direct ? 1 : 0;
   p.out = a.out;
+  p.ldo = static_cast<int>(ldo);
+  p.n_peers = a.n_peers;
+  for (int i = 0; i < kMaxPeers; ++i) p.peers[i] = i < a.n_peers ? a.peers[i] : nullptr;
+  if (a.n_peers > 0 && direct) {
+    set_error("fp8_gemm: peer outputs need 16-byte rows (N and the row pitch multiples of 8, "
+              "16-byte aligned buffers)");
+    return 2;
+  }
   p.pdl = pdl ? 1 : 0;
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
   if (tiles > 0x7fffffffLL) {
@@ -599,8 +640,9 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
               std::to_string(dev.cc_major) + std::to_string(dev.cc_minor));
     return 5;
   }
-  if (a.M > 0x7fffffffLL || a.N > 0x7fffffffLL || a.K > 0x7fffffffLL) {
-    set_error("fp8_gemm: dimensions must fit in int32");
+  if (a.M > 0x7fffffffLL || a.N > 0x7fffffffLL || a.K > 0x7fffffffLL || a.ldo > 0x7fffffffLL ||
+      a.n_peers < 0 || a.n_peers > kMaxPeers) {
+    set_error("fp8_gemm: dimensions must fit in int32 and at most 7 peers");
     return 2;
   }
   // One 128-row tile per SM when M fits in it; CTA pairs with 256-row tiles otherwise.

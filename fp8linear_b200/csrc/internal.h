@@ -49,7 +49,15 @@ struct GemmArgs {
   void *out;
   int out_dtype;
   int64_t M, N, K;
+  // Output row pitch in elements (0: N). With ldo > N the output is a column block of
+  // a wider matrix, `out` pointing at the block's first column.
+  int64_t ldo = 0;
+  // Copies of the output block written to other GPUs' buffers (peer-mapped pointers,
+  // same layout as `out`), straight from the epilogue.
+  int n_peers = 0;
+  void *const *peers = nullptr;
 };
+constexpr int kMaxPeers = 7;
 // Launches the tcgen05 GEMM + fused epilogue. `pdl` launches it as a programmatic
 // dependent of the previous kernel on the stream. Returns an fp8lin_status code and
 // sets the error message on failure.

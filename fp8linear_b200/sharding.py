@@ -80,3 +80,44 @@ def column_parallel_linear(x: torch.Tensor, wq_shard: torch.Tensor, ws_shard: to
     if world == 1:
         return local
     return gather_columns(local, world, group)
+
+
+class FusedColumnParallel:
+    """N-shard linear with the all-gather fused into the GEMM epilogue.
+
+    Every rank owns an [M, N_total] output buffer in symmetric memory (mapped into every
+    other rank's address space). ``__call__`` runs the fused op on this rank's channel
+    block: each output box is stored to this GPU's buffer and, with P2P stores over
+    NVLink, to every peer's buffer at this rank's column offset; a one-element NCCL
+    all-reduce then orders every rank's writes before anyone reads the result. No
+    separate all-gather or interleave copy runs.
+    """
+
+    def __init__(self, M: int, N_total: int, dtype: torch.dtype, device: torch.device,
+                 group=None):
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.M, self.N_total = M, N_total
+        column_range(N_total, self.world, self.rank)  # validates the split
+        self.buf = symm.empty(M, N_total, dtype=dtype, device=device)
+        self.hdl = symm.rendezvous(self.buf, self.group)
+        offset = self.buf.data_ptr() - self.hdl.buffer_ptrs[self.rank]
+        self.bases = [int(b) + offset for b in self.hdl.buffer_ptrs]
+        self.flag = torch.zeros(1, device=device)
+
+    def out_ptrs(self) -> list[int]:
+        """This rank's first output column in every rank's buffer, own buffer first."""
+        n_local = self.N_total // self.world
+        col = self.rank * n_local * self.buf.element_size()
+        order = [self.rank] + [r for r in range(self.world) if r != self.rank]
+        return [self.bases[r] + col for r in order]
+
+    def __call__(self, x, wq_shard, ws_shard, bias_shard, capi, workspace=None):
+        capi.fp8_linear_allgather(x, wq_shard, ws_shard, bias_shard, self.out_ptrs(),
+                                  ldo=self.N_total, workspace=workspace)
+        if self.world > 1:
+            dist.all_reduce(self.flag, group=self.group)
+        return self.buf

@@ -126,6 +126,27 @@ FP8LIN_API int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq,
                                  void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Column-parallel FP8 linear with the output all-gather fused into the GEMM epilogue
+ * (the N-shard of the multi-GPU split; no reference counterpart, the reference has no
+ * multi-GPU code). This rank holds N output channels (wq/w_scale/bias rows) of a wider
+ * [M, ldo] output; each output box the epilogue produces is written to outs[0] (this
+ * GPU, TMA store) and to outs[1..n_outs-1] (other GPUs' buffers mapped into this process,
+ * e.g. peer or symmetric memory, with 16-byte P2P stores), so the gather overlaps the
+ * math and no separate collective or interleave copy runs.
+ *   outs[i]: pointer to this rank's first output column in buffer i; rows of ldo
+ *            elements; all buffers 16-byte aligned; N and ldo multiples of 8
+ *   n_outs:  1..8 (1 = this GPU only)
+ * Other arguments as fp8lin_fp8_linear. The caller orders the peers' reads after every
+ * rank's call completes (e.g. a device-side barrier on the stream).
+ */
+FP8LIN_API int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq,
+                                           const float *w_scale, const void *bias,
+                                           int bias_dtype, void *const *outs, int n_outs,
+                                           int out_dtype, int64_t M, int64_t N, int64_t K,
+                                           int64_t ldo, void *workspace,
+                                           size_t workspace_bytes, void *stream);
+
+/*
  * Size of the device scratch array fp8lin_fp8_linear_noalloc works in (64 MiB).
  * Every GPU that loads the library holds this array until the process exits.
  */
