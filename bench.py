@@ -419,18 +419,28 @@ def measure_workload(name: str, steps: int, warmup: int) -> dict:
     stream = torch.cuda.current_stream(dev)
 
     def timed(fn):
+        # The op is captured in a CUDA graph and replayed, so the timed window holds
+        # device work only (for microsecond-scale kernels the host cost of an eager op
+        # call can exceed the flush and leave the GPU idle inside the window).
         for _ in range(warmup):
             flush.zero_()
             fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(2):
+            g.replay()
         evs = []
         for _ in range(steps):
             flush.zero_()
             a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            fn()
+            g.replay()
             c.record(stream)
             evs.append((a, c))
         torch.cuda.synchronize(dev)
+        del g
         return statistics.median(a.elapsed_time(c) for a, c in evs)
 
     fused = timed(lambda: f.fp8_linear(x, wq, ws, b))

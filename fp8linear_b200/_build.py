@@ -32,7 +32,7 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-KERNEL_SOURCES = ["quantize.cu", "gemm_sm100.cu", "capi.cu", "noalloc.cu"]
+KERNEL_SOURCES = ["quantize.cu", "gemm_sm100.cu", "gemm_small_sm100.cu", "capi.cu", "noalloc.cu"]
 HEADERS = ["ptx.cuh", "internal.h"]
 
 

@@ -229,12 +229,13 @@ int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, cons
 int fp8lin_device_status(unsigned int *status, int clear) {
   clear_error();
   if (!status) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "device_status: null pointer");
-  unsigned int q = 0;
+  unsigned int q = 0, sm = 0;
   cudaError_t e = read_gemm_status(status, clear != 0);
   if (e == cudaSuccess) e = read_quant_status(&q, clear != 0);
+  if (e == cudaSuccess) e = read_small_status(&sm, clear != 0);
   if (e != cudaSuccess)
     return fail(FP8LIN_ERR_CUDA, std::string("device_status: ") + cudaGetErrorString(e));
-  *status |= q;
+  *status |= q | sm;
   return FP8LIN_OK;
 }
 

@@ -631,6 +631,12 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
 
 }  // namespace gemm
 
+bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                     uint32_t box_inner, uint32_t box_outer, std::string *err) {
+  return gemm::make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, inner, outer, inner,
+                            box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_128B, err);
+}
+
 int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   if (a.M == 0 || a.N == 0) return 0;
   DeviceInfo dev;
@@ -645,7 +651,9 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     set_error("fp8_gemm: dimensions must fit in int32 and at most 7 peers");
     return 2;
   }
-  // One 128-row tile per SM when M fits in it; CTA pairs with 256-row tiles otherwise.
+  // Few tokens: stream the weights with swap-AB split-K tiles. Otherwise CTA pairs with
+  // 256-row tiles (or single CTAs with 128-row tiles for peer outputs at M <= 128).
+  if (a.M <= gemm::BM && a.n_peers == 0) return launch_gemm_small(a, stream, pdl);
   if (a.M <= gemm::BM) return gemm::launch_shape<1>(a, dev, stream, pdl);
   return gemm::launch_shape<2>(a, dev, stream, pdl);
 }

@@ -1,0 +1,375 @@
+// gemm_small_sm100.cu -- the FP8 GEMM + fused dequant/bias epilogue for few tokens
+// (M <= 128), where the work is streaming the weight matrix once.
+//
+// Same result as fp8_gemm_kernel (out[m,n] = fma(acc * x_scale[m], w_scale[n], bias[n]),
+// acc = e4m3 dot products accumulated in fp32), organised for a weight-bandwidth-bound
+// shape:
+//  * swap-AB: the MMA computes D^T = W . X^T, so 128 weight rows fill the tensor core's
+//    M = 128 and the tokens (padded to a multiple of 16) are its N, instead of 127 of 128
+//    MMA rows multiplying zero padding;
+//  * split-K over a thread-block cluster of S CTAs (grid = ceil(N/128) x S, about one
+//    CTA per SM): CTA r of a cluster streams K-blocks [r*kps, (r+1)*kps) of a 128-row
+//    weight tile, so every SM pulls a slice of the weights;
+//  * the S partial tiles meet in distributed shared memory: each CTA parks its fp32
+//    partial [tokens x 128] in its own shared memory, and after a cluster barrier CTA r
+//    reduces rows [r*R, (r+1)*R) of the tile over all S CTAs (fixed order, so the result
+//    is deterministic), applies the scales and bias and writes bf16 (or fp16).
+// Warp roles as in the large kernel: warp 0 TMA producer, warp 1 MMA issuer (+ TMEM
+// owner), warps 2-5 move the accumulator from TMEM to shared memory; all warps reduce.
+// Every mbarrier wait is bounded; a wait that runs out sets bit 16 of this file's
+// watchdog word (read with the others by fp8lin_device_status) and the CTA winds down.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace fp8lin {
+
+__device__ unsigned int g_small_status;  // watchdog bits (16 = small-M GEMM wait ran out)
+
+namespace small {
+
+constexpr int WN = 128;        // weight rows per CTA = MMA M
+constexpr int BK = 128;        // bytes (= e4m3 elements) per K-block
+constexpr int UMMA_K = 32;
+constexpr int MAX_TOK = 128;   // tokens per launch (MMA N after padding)
+constexpr int STAGES = 4;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t W_STAGE = WN * BK;                     // 16 KB
+constexpr uint32_t X_STAGE_MAX = MAX_TOK * BK;            // 16 KB
+constexpr uint32_t STAGE_MAX = W_STAGE + X_STAGE_MAX;
+constexpr uint32_t PART_MAX = MAX_TOK * WN * 4;           // fp32 partial tile, 64 KB
+constexpr uint32_t OFF_PART = STAGES * STAGE_MAX;         // 128 KB
+constexpr uint32_t OFF_BAR = OFF_PART + PART_MAX;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + (2 * STAGES + 2) * 8 + 16 + 1024;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint64_t kDrainLimitNs = 1000000000ull;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+struct Params {
+  const float *xs;
+  const float *ws;
+  const void *bias;
+  int bias_dtype;
+  void *out;
+  int out_dtype;
+  int M, N, K, ldo;
+  int mpad;          // tokens padded to a multiple of 16 (MMA N)
+  int k_blocks;
+  int split;         // cluster size = K-splits per weight tile
+  int kps;           // K-blocks per split
+  uint32_t idesc;
+  uint32_t tmem_cols;
+  int pdl;
+};
+
+__device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
+  switch (dtype) {
+    case kBF16: {
+      const uint16_t b = __ldg(reinterpret_cast<const unsigned short *>(bias) + n);
+      return __uint_as_float(static_cast<uint32_t>(b) << 16);
+    }
+    case kF16: return __half2float(__ldg(reinterpret_cast<const __half *>(bias) + n));
+    case kF32: return __ldg(reinterpret_cast<const float *>(bias) + n);
+    default: return 0.0f;
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fp8_gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                          const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const uint32_t x_stage = static_cast<uint32_t>(p.mpad) * BK;
+  const uint32_t stage_bytes = W_STAGE + x_stage;  // multiple of 2 KB
+  const uint32_t bar_full = sbase + OFF_BAR;
+  const uint32_t bar_empty = bar_full + 8 * STAGES;
+  const uint32_t bar_acc = bar_empty + 8 * STAGES;
+  const uint32_t bar_drain = bar_acc + 8;
+  volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + OFF_BAR +
+                                                                       (2 * STAGES + 2) * 8);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + OFF_BAR + (2 * STAGES + 2) * 8 + 4);
+  float *part = reinterpret_cast<float *>(smem + OFF_PART);  // [mpad][WN]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();  // K-split index
+  const int tile = blockIdx.x / p.split;         // 128-row weight tile
+  const int kb0 = static_cast<int>(rank) * p.kps;
+  const int kb1 = min(p.k_blocks, kb0 + p.kps);
+  const int nkb = kb1 - kb0;  // >= 1 (host guarantees)
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&tmap_w);
+    ptx::prefetch_tmap(&tmap_x);
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(bar_full + 8 * s, 1);
+      ptx::mbar_init(bar_empty + 8 * s, 1);
+    }
+    ptx::mbar_init(bar_acc, 1);
+    ptx::mbar_init(bar_drain, 1);
+    *abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t *>(tmem_slot)), p.tmem_cols);
+    ptx::tmem_relinquish<1>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (p.pdl) ptx::grid_dependency_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
+        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kWaitLimitNs)) {
+          if (!*abort) {
+            atomicOr(&g_small_status, 16u);
+            *abort = 1;
+          }
+          break;
+        }
+        const uint32_t fb = bar_full + 8 * s;
+        const uint32_t dst = sbase + static_cast<uint32_t>(s) * stage_bytes;
+        ptx::mbar_arrive_expect_tx(fb, stage_bytes);
+        ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
+        ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, 0, fb);
+        ++issued;
+      }
+      for (int i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
+        ptx::mbar_wait_timeout(bar_empty + 8 * (i % STAGES),
+                               static_cast<uint32_t>(i / STAGES) & 1u, kDrainLimitNs);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
+        if (!ptx::mbar_wait_bounded(bar_full + 8 * s, ph, abort, kWaitLimitNs)) {
+          if (!*abort) {
+            atomicOr(&g_small_status, 16u);
+            *abort = 1;
+          }
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t st = sbase + static_cast<uint32_t>(s) * stage_bytes;
+        const uint64_t adesc = ptx::sw128_kmajor_desc(st);
+        const uint64_t bdesc = ptx::sw128_kmajor_desc(st + W_STAGE);
+#pragma unroll
+        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+          const uint64_t koff = static_cast<uint64_t>((kk * UMMA_K) >> 4);
+          ptx::mma_f8f6f4(tmem, adesc + koff, bdesc + koff, p.idesc, (i | kk) != 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(bar_empty + 8 * s);
+      }
+      if (ok) ptx::mma_commit(bar_acc);
+      ptx::mma_commit(bar_drain);
+      ptx::mbar_wait_timeout(bar_drain, 0, kDrainLimitNs);
+    }
+  } else {
+    // TMEM (lane = weight row, column = token) -> part[token][row], fp32
+    const int quarter = warp & 3;
+    const bool ok = ptx::mbar_wait_bounded(bar_acc, 0, abort, kWaitLimitNs);
+    if (!ok && lane == 0 && !*abort) {
+      atomicOr(&g_small_status, 16u);
+      *abort = 1;
+    }
+    ptx::tc_fence_after();
+    const int row = quarter * 32 + lane;
+    for (int c = 0; c < p.mpad; c += 16) {
+      uint32_t r[16];
+      if (ok) {
+        ptx::tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                    static_cast<uint32_t>(c),
+                                r);
+        ptx::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) part[(c + j) * WN + row] = __uint_as_float(r[j]);
+    }
+    ptx::tc_fence_before();
+  }
+
+  __syncwarp();
+  __syncthreads();
+  ptx::cluster_sync();  // every CTA's partial tile is in its shared memory
+
+  // CTA `rank` reduces tile rows [r0, r1) (a multiple of 4 wide) over the cluster's
+  // partials and writes out. Each task is 4 consecutive rows of one token: the loads from
+  // all ranks' shared memory are issued together, then summed in rank order.
+  const int R = ((WN + p.split - 1) / p.split + 3) & ~3;
+  const int r0 = static_cast<int>(rank) * R;
+  const int r1 = min(WN, r0 + R);
+  const int quads = r1 > r0 ? (r1 - r0) >> 2 : 0;
+  const uint32_t part_base = ptx::smem_u32(part);
+  for (int idx = threadIdx.x; idx < p.M * quads; idx += NUM_THREADS) {
+    const int m = idx / quads;
+    const int nl = r0 + 4 * (idx - m * quads);
+    const uint32_t off = static_cast<uint32_t>(m * WN + nl) * 4u;
+    float4 v[8];
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2)
+      if (s2 < p.split) v[s2] = ptx::ld_shared_cluster_v4(ptx::map_shared_rank(part_base + off, s2));
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2)
+      if (s2 < p.split) {
+        acc[0] += v[s2].x;
+        acc[1] += v[s2].y;
+        acc[2] += v[s2].z;
+        acc[3] += v[s2].w;
+      }
+    const float xs = __ldg(p.xs + m);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int n = tile * WN + nl + e;
+      if (n >= p.N) break;
+      const float val = fmaf(acc[e] * xs, __ldg(p.ws + n),
+                             p.bias_dtype != kNone ? load_bias(p.bias, p.bias_dtype, n) : 0.0f);
+      const int64_t o = static_cast<int64_t>(m) * p.ldo + n;
+      if (p.out_dtype == kF16)
+        reinterpret_cast<__half *>(p.out)[o] = __float2half_rn(val);
+      else
+        reinterpret_cast<__nv_bfloat16 *>(p.out)[o] = __float2bfloat16_rn(val);
+    }
+  }
+
+  ptx::cluster_sync();  // peers may still be reading this CTA's partial tile
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<1>(tmem, p.tmem_cols);
+  }
+}
+
+}  // namespace small
+
+bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                     uint32_t box_inner, uint32_t box_outer, std::string *err);
+
+int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
+  using namespace small;
+  DeviceInfo dev;
+  if (!current_device_info(&dev)) return 5;
+  std::string err;
+  const int mpad = static_cast<int>((a.M + 15) / 16 * 16);
+  CUtensorMap tw, tx;
+  if (!make_tmap_2d_u8(&tw, a.wq, a.K, a.N, BK, WN, &err) ||
+      !make_tmap_2d_u8(&tx, a.xq, a.K, a.M, BK, mpad, &err)) {
+    set_error("fp8_gemm: " + err);
+    return 4;
+  }
+  Params p;
+  p.xs = a.xs;
+  p.ws = a.ws;
+  p.bias = a.bias;
+  p.bias_dtype = a.bias ? a.bias_dtype : kNone;
+  p.out = a.out;
+  p.out_dtype = a.out_dtype;
+  p.M = static_cast<int>(a.M);
+  p.N = static_cast<int>(a.N);
+  p.K = static_cast<int>(a.K);
+  p.ldo = static_cast<int>(a.ldo > 0 ? a.ldo : a.N);
+  p.mpad = mpad;
+  p.k_blocks = static_cast<int>((a.K + BK - 1) / BK);
+  const int tiles = static_cast<int>((a.N + WN - 1) / WN);
+
+  static std::once_flag once[64];
+  cudaError_t ce = cudaSuccess;
+  static int max_clusters[64][9];  // co-resident clusters per cluster size, per device
+  std::call_once(once[dev.device & 63], [&] {
+    ce = cudaFuncSetAttribute(fp8_gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(SMEM_BYTES));
+    for (int c = 1; c <= 8 && ce == cudaSuccess; ++c) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(c);
+      q.blockDim = dim3(NUM_THREADS);
+      q.dynamicSmemBytes = SMEM_BYTES;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = c;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      q.attrs = at;
+      q.numAttrs = 1;
+      int n = 0;
+      ce = cudaOccupancyMaxActiveClusters(&n, fp8_gemm_small_kernel, &q);
+      max_clusters[dev.device & 63][c] = n;
+    }
+  });
+  if (ce != cudaSuccess) {
+    set_error(std::string("fp8_gemm: small kernel setup: ") + cudaGetErrorString(ce));
+    return 4;
+  }
+  // K-splits (= cluster size): the largest, at most 8, whose co-resident clusters hold
+  // every weight tile in one wave; each split at least one K-block.
+  int split = 1;
+  for (int c = std::min(8, p.k_blocks); c >= 1; --c)
+    if (max_clusters[dev.device & 63][c] >= tiles) {
+      split = c;
+      break;
+    }
+  p.kps = (p.k_blocks + split - 1) / split;
+  split = (p.k_blocks + p.kps - 1) / p.kps;
+  p.split = split;
+  p.idesc = ptx::idesc_e4m3_f32(WN, mpad);
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(mpad)) cols <<= 1;
+  p.tmem_cols = cols;
+  p.pdl = pdl ? 1 : 0;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * split);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  int n = 1;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  ce = cudaLaunchKernelEx(&cfg, fp8_gemm_small_kernel, tw, tx, p);
+  if (ce != cudaSuccess) {
+    set_error(std::string("fp8_gemm: small kernel launch failed: ") + cudaGetErrorString(ce));
+    return 4;
+  }
+  return 0;
+}
+
+cudaError_t read_small_status(unsigned int *bits, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(bits, g_small_status, sizeof(unsigned int));
+  if (e != cudaSuccess) return e;
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_small_status, &zero, sizeof(unsigned int));
+  }
+  return e;
+}
+
+}  // namespace fp8lin

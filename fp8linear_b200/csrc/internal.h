@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <string>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace fp8lin {
@@ -64,5 +65,12 @@ constexpr int kMaxPeers = 7;
 int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl);
 // Reads (and optionally clears) the GEMM watchdog bits of the current device.
 cudaError_t read_gemm_status(unsigned int *bits, bool clear);
+
+// ---- gemm_small_sm100.cu (M <= 128: swap-AB, split-K over a cluster)
+int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl);
+cudaError_t read_small_status(unsigned int *bits, bool clear);
+// 2-D uint8 tensor map with 128-byte swizzle (shared by both GEMM shapes).
+bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                     uint32_t box_inner, uint32_t box_outer, std::string *err);
 
 }  // namespace fp8lin

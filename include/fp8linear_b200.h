@@ -177,7 +177,8 @@ FP8LIN_API int fp8lin_fp8_linear_noalloc(const void *x, int x_dtype, const void 
 /*
  * Watchdog status of the kernels on the current device: every wait in them is
  * bounded; a wait that runs out sets a bit here and the kernel returns early instead
- * of hanging (GEMM: 1 = TMA producer, 2 = MMA issuer, 4 = epilogue; 8 = quantizer).
+ * of hanging (GEMM: 1 = TMA producer, 2 = MMA issuer, 4 = epilogue; 8 = quantizer;
+ * 16 = few-token GEMM).
  * *status receives the bits; clear != 0 resets them. Synchronous on the device.
  * No counterpart in the reference (cuBLASLt has no such report).
  */
