@@ -31,6 +31,7 @@ SIGNATURES = {
     "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
     "fp8lin_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
     "fp8lin_fp8_linear_noalloc": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
+    "fp8lin_selftest_watchdog": (_I, [ctypes.c_uint, ctypes.POINTER(ctypes.c_uint), _P]),
     "fp8lin_fp8_linear_allgather": (_I, [_P, _I, _P, _P, _P, _I, ctypes.POINTER(ctypes.c_void_p),
                                          _I, _I, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
 }
@@ -147,6 +148,14 @@ class CApi:
             arr, len(out_ptrs), DTYPE[out_dtype], M, N, K, ldo, workspace.data_ptr(),
             workspace.numel(), self._stream(x))
         self._check(rc, "fp8lin_fp8_linear_allgather")
+
+    def selftest_watchdog(self, limit_us: int = 50_000) -> int:
+        """Run the bounded-wait self-test; returns the recorded status (32 = the wait ran
+        out and the kernel returned cleanly)."""
+        v = ctypes.c_uint(0)
+        self._check(self.lib.fp8lin_selftest_watchdog(limit_us, ctypes.byref(v), self._stream()),
+                    "fp8lin_selftest_watchdog")
+        return int(v.value)
 
     def device_status(self, clear: bool = False) -> int:
         v = ctypes.c_uint(0)

@@ -226,6 +226,17 @@ int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, cons
   return launch_gemm(a, s, true);
 }
 
+int fp8lin_selftest_watchdog(unsigned int limit_us, unsigned int *status, void *stream) {
+  clear_error();
+  if (!status) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "selftest_watchdog: null status");
+  if (limit_us == 0 || limit_us > 1000000u)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "selftest_watchdog: limit must be 1..1000000 us");
+  cudaError_t e = launch_watchdog_selftest(limit_us, status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("selftest_watchdog: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
 int fp8lin_device_status(unsigned int *status, int clear) {
   clear_error();
   if (!status) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "device_status: null pointer");

@@ -658,6 +658,37 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   return gemm::launch_shape<2>(a, dev, stream, pdl);
 }
 
+namespace {
+__device__ unsigned int g_selftest_result;
+
+// One thread waits on a barrier whose single expected arrival never comes, through the
+// same bounded wait the GEMM uses; the run-out is recorded and the kernel returns.
+__global__ void watchdog_selftest_kernel(uint64_t limit_ns) {
+  __shared__ alignas(8) uint64_t bar;
+  __shared__ int abort_flag;
+  const uint32_t b = ptx::smem_u32(&bar);
+  ptx::mbar_init(b, 1);
+  abort_flag = 0;
+  ptx::fence_mbar_init();
+  const bool done = ptx::mbar_wait_bounded(b, 0, &abort_flag, limit_ns);
+  g_selftest_result = done ? 0u : 32u;
+}
+}  // namespace
+
+cudaError_t launch_watchdog_selftest(unsigned int limit_us, unsigned int *status,
+                                     cudaStream_t stream) {
+  const unsigned int zero = 0xFFFFFFFFu;
+  cudaError_t e = cudaMemcpyToSymbolAsync(g_selftest_result, &zero, sizeof(zero), 0,
+                                          cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return e;
+  watchdog_selftest_kernel<<<1, 1, 0, stream>>>(static_cast<uint64_t>(limit_us) * 1000ull);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  e = cudaMemcpyFromSymbolAsync(status, g_selftest_result, sizeof(unsigned int), 0,
+                                cudaMemcpyDeviceToHost, stream);
+  if (e != cudaSuccess) return e;
+  return cudaStreamSynchronize(stream);
+}
+
 cudaError_t read_gemm_status(unsigned int *bits, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(bits, g_gemm_status, sizeof(unsigned int));
   if (e != cudaSuccess) return e;

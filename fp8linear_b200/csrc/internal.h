@@ -66,6 +66,12 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl);
 // Reads (and optionally clears) the GEMM watchdog bits of the current device.
 cudaError_t read_gemm_status(unsigned int *bits, bool clear);
 
+// Launches one thread that waits, bounded by `limit_us`, on an mbarrier nothing arrives
+// on (the watchdog path every kernel's waits share) and copies the outcome to the host:
+// *status = 32 when the wait ran out and the kernel returned. Synchronous.
+cudaError_t launch_watchdog_selftest(unsigned int limit_us, unsigned int *status,
+                                     cudaStream_t stream);
+
 // ---- gemm_small_sm100.cu (M <= 128: swap-AB, split-K over a cluster)
 int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl);
 cudaError_t read_small_status(unsigned int *bits, bool clear);

@@ -184,6 +184,15 @@ FP8LIN_API int fp8lin_fp8_linear_noalloc(const void *x, int x_dtype, const void 
  */
 FP8LIN_API int fp8lin_device_status(unsigned int *status, int clear);
 
+/*
+ * Exercises the watchdog on the GPU without a fault: one thread waits, through the same
+ * bounded wait every kernel here uses, on an mbarrier that nothing arrives on, for
+ * limit_us microseconds (1..1000000); the wait runs out, the kernel records it and
+ * returns, and *status receives 32. Synchronous on `stream`. No reference counterpart.
+ */
+FP8LIN_API int fp8lin_selftest_watchdog(unsigned int limit_us, unsigned int *status,
+                                        void *stream);
+
 #ifdef __cplusplus
 }
 #endif
