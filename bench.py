@@ -12,11 +12,14 @@ replicated and no collective; each rank runs its own M-row batch (weak scaling) 
 ``value`` is the FLOPs of all ranks over the max-over-ranks device time.
 
 Timing: W untimed warm-up steps, then exactly K timed steps between a barrier and a
-device synchronize; each step is bracketed by CUDA events on the launching stream and
-a 256 MiB buffer is written between steps (more than the 126 MB L2), so every step
-reads its operands from HBM. ``e2e`` repeats the step through the C ABI with the
-activations copied from pinned host memory and the output copied back inside the
-timed region. ``roofline`` times the GEMM kernel alone over K further launches.
+device synchronize, on the device with two CUDA events on the launching stream. The K
+steps run back to back from one CUDA graph (no host gaps between kernels) and cycle
+over several independent operand sets (activations, weights, outputs) whose combined
+size is a few times the 126 MB L2, so every step reads operands that were evicted
+since their last use. ``e2e`` repeats the step through the C ABI with the activations
+copied from pinned host memory and the output copied back inside the timed region.
+``roofline`` and ``quantizer`` time the GEMM kernel and the quantizer alone the same
+way (K launches over the rotating sets; average device time per launch).
 ``cpu_baseline`` times the CPU restatement of the reference path (the oracle port:
 per-token e4m3 quant, fp32 matmul, dequant + bias) on a bounded row sample.
 
@@ -46,6 +49,7 @@ METRIC = "FP8 linear TFLOP/s at FLUX shapes vs 4.5 PF peak; quant GB/s vs 8 TB/s
 FLUSH_BYTES = 256 << 20
 NOMINAL_FP8_TFLOPS = 4500.0
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_FALLBACK = 126 << 20
 
 
 # ----------------------------------------------------------------------------- plumbing
@@ -174,6 +178,78 @@ class ClockSampler:
                 "reasons": sorted(reasons), "source": source}
 
 
+# ----------------------------------------------------------------------------- timing
+
+
+def l2_bytes(dev) -> int:
+    return int(getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 0) or L2_FALLBACK)
+
+
+def set_count(per_set_bytes: int, dev, lo: int = 3, hi: int = 512) -> int:
+    """Operand sets to rotate over so that, between two uses of one set, the others
+    touch at least 3x the L2 capacity (its lines are evicted by then)."""
+    need = -(-3 * l2_bytes(dev) // max(1, per_set_bytes))
+    return max(lo, min(hi, need))
+
+
+def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True):
+    """``n_sets`` independent (x, wq, ws, bias[, xq, xs]) sets of workload ``wl`` on
+    the current device (weights quantized once, as offline). Set i's weight depends
+    only on i, so ranks hold the same weights; activations use ``x_seed0``."""
+    import fp8linear_b200 as f
+    from fp8linear_b200.workloads import make_weight, make_x
+
+    sets = []
+    for i in range(n_sets):
+        x = make_x(wl, seed=x_seed0 + 7919 * i, gen_device="cuda")
+        w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
+        wq, ws = f.quantize_weight(w)
+        del w
+        s = {"x": x, "wq": wq, "ws": ws, "b": b}
+        if quantize_x:
+            s["xq"], s["xs"] = f.quantize_fp8(x)
+        sets.append(s)
+    return sets
+
+
+def per_set_bytes(wl) -> int:
+    """HBM bytes one step's operand set occupies: x, codes + scales, weight codes +
+    scales + bias, output."""
+    return (2 * wl.M * wl.K + wl.M * wl.K + 4 * wl.M + wl.N * wl.K + 4 * wl.N + 2 * wl.N
+            + 2 * wl.M * wl.N)
+
+
+def graph_launches(call, sets, reps: int, keep: int):
+    """A CUDA graph of ``reps`` calls cycling over ``sets``. The outputs of the last
+    ``keep`` calls stay referenced during capture, so consecutive calls write distinct
+    buffers (like consecutive layers) instead of one recycled block."""
+    from collections import deque
+
+    for st in sets:  # eager first calls (per-device setup) outside the capture
+        call(st)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    live = deque(maxlen=max(1, keep))
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            live.append(call(sets[i % len(sets)]))
+    live.clear()
+    return g
+
+
+def time_graph(g, stream, barrier) -> float:
+    """Device milliseconds of one replay of ``g``: a barrier and a synchronize on both
+    sides, CUDA events on the launching stream."""
+    g.replay()  # untimed replay: warm
+    barrier()
+    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    g.replay()
+    c.record(stream)
+    barrier()
+    return a.elapsed_time(c)
+
+
 # ----------------------------------------------------------------------------- CPU path
 
 
@@ -234,19 +310,20 @@ def run_gpu(args):
 
     import fp8linear_b200 as f
     from fp8linear_b200.capi import CApi
-    from fp8linear_b200.workloads import WORKLOADS, make_weight, make_x
+    from fp8linear_b200.workloads import WORKLOADS
 
     wl = WORKLOADS[args.workload]
     M, K, N = wl.M, wl.K, wl.N
-    x = make_x(wl, seed=rank, gen_device="cuda")          # this rank's shard of token rows
-    w, b = make_weight(wl, gen_device="cuda")              # replicated weight
-    wq, ws = f.quantize_weight(w)
-    del w
+    per_set = per_set_bytes(wl)
+    n_sets = set_count(per_set, dev)
+    # this rank's token rows (its own seeds) and a replicated weight per set
+    sets = operand_sets(wl, n_sets, x_seed0=1000 * rank)
+    x, wq, ws, b = sets[0]["x"], sets[0]["wq"], sets[0]["ws"], sets[0]["b"]
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
-        return f.fp8_linear(x, wq, ws, b)
+    def step(st):
+        return f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"])
 
     def barrier():
         if world > 1:
@@ -255,23 +332,14 @@ def run_gpu(args):
 
     # ---- warm-up (the clock sampler starts here: the GPU is busy from now on)
     clocks = ClockSampler(local).start()
-    for _ in range(args.warmup):
-        flush.zero_()
-        step()
+    for i in range(args.warmup):
+        step(sets[i % n_sets])
     barrier()
 
-    # ---- timed: K fused steps, L2 flushed between steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    barrier()
-    for i in range(args.steps):
-        flush.zero_()
-        ev[i][0].record(stream)
-        step()
-        ev[i][1].record(stream)
-    barrier()
-    step_ms = [a.elapsed_time(b_) for a, b_ in ev]
-    total_ms = sum(step_ms)
+    # ---- timed: K fused steps back to back over the rotating operand sets
+    g_step = graph_launches(step, sets, args.steps, keep=n_sets)
+    total_ms = time_graph(g_step, stream, barrier)
+    del g_step
     if world > 1:
         t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -280,25 +348,14 @@ def run_gpu(args):
     value = world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12
     ms_per_step = total_ms / args.steps
 
-    # ---- roofline: GEMM kernel and quantizer timed alone (same stream, events per launch)
-    xq, xs = f.quantize_fp8(x)
-    gemm_ms, quant_ms = [], []
-    for i in range(args.steps):
-        flush.zero_()
-        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        e0.record(stream)
-        f.quantize_fp8(x)
-        e1.record(stream)
-        flush.zero_()
-        e1b = torch.cuda.Event(enable_timing=True)
-        e1b.record(stream)
-        f.fp8_gemm(xq, xs, wq, ws, b)
-        e2.record(stream)
-        gemm_ms.append((e1b, e2))
-        quant_ms.append((e0, e1))
-    torch.cuda.synchronize(dev)
-    g_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in gemm_ms)
-    q_ms = statistics.mean(a.elapsed_time(b_) for a, b_ in quant_ms)
+    # ---- roofline: GEMM kernel and quantizer alone, K launches each, same rotation
+    g_gemm = graph_launches(lambda st: f.fp8_gemm(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]),
+                            sets, args.steps, keep=n_sets)
+    g_ms = time_graph(g_gemm, stream, barrier) / args.steps
+    del g_gemm
+    g_quant = graph_launches(lambda st: f.quantize_fp8(st["x"]), sets, args.steps, keep=n_sets)
+    q_ms = time_graph(g_quant, stream, barrier) / args.steps
+    del g_quant
     pk = peaks()
     fp8_peak = 2.0 * pk["bf16_tflops"]
     gemm_tflops = flops_rank / (g_ms * 1e-3) / 1e12
@@ -375,7 +432,9 @@ def run_gpu(args):
             "config": {"workload": wl.name, "M_per_gpu": M, "K": K, "N": N,
                        "global_tokens": M * world, "x": "bf16", "out": "bf16",
                        "parallelism": f"M-shard x{world}, weights replicated, no collective",
-                       "l2": "flushed between steps (256 MiB write)"},
+                       "l2": f"inputs larger than L2: {n_sets} rotating operand sets of "
+                             f"{per_set / 1e6:.0f} MB (x, weight, output); steps back to back "
+                             f"in one CUDA graph"},
             "roofline": {"bound": "tensor", "kernel": "fp8_gemm_kernel",
                          "achieved": round(gemm_tflops, 1), "peak": round(fp8_peak, 1),
                          "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
@@ -404,54 +463,35 @@ def run_gpu(args):
 
 def measure_workload(name: str, steps: int, warmup: int) -> dict:
     """Per-workload device times of the fused op, the GEMM alone and the quantizer
-    alone (CUDA events, L2 flushed before every timed launch)."""
+    alone: each is ``max(steps, sets)`` launches back to back in one CUDA graph over
+    rotating operand sets (inputs larger than L2), averaged per launch."""
     import fp8linear_b200 as f
-    from fp8linear_b200.workloads import WORKLOADS, make_weight, make_x
+    from fp8linear_b200.workloads import WORKLOADS
 
     wl = WORKLOADS[name]
     dev = torch.device("cuda", torch.cuda.current_device())
-    x = make_x(wl, gen_device="cuda")
-    w, b = make_weight(wl, gen_device="cuda")
-    wq, ws = f.quantize_weight(w)
-    del w
-    xq, xs = f.quantize_fp8(x)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    n_sets = set_count(per_set_bytes(wl), dev)
+    sets = operand_sets(wl, n_sets)
     stream = torch.cuda.current_stream(dev)
+    reps = max(steps, n_sets)
 
-    def timed(fn):
-        # The op is captured in a CUDA graph and replayed, so the timed window holds
-        # device work only (for microsecond-scale kernels the host cost of an eager op
-        # call can exceed the flush and leave the GPU idle inside the window).
-        for _ in range(warmup):
-            flush.zero_()
-            fn()
-        torch.cuda.synchronize(dev)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            fn()
-        for _ in range(2):
-            g.replay()
-        evs = []
-        for _ in range(steps):
-            flush.zero_()
-            a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            g.replay()
-            c.record(stream)
-            evs.append((a, c))
-        torch.cuda.synchronize(dev)
+    def timed(call):
+        for i in range(warmup):
+            call(sets[i % n_sets])
+        g = graph_launches(call, sets, reps, keep=n_sets)
+        ms = time_graph(g, stream, lambda: torch.cuda.synchronize(dev)) / reps
         del g
-        return statistics.median(a.elapsed_time(c) for a, c in evs)
+        return ms
 
-    fused = timed(lambda: f.fp8_linear(x, wq, ws, b))
-    gemm = timed(lambda: f.fp8_gemm(xq, xs, wq, ws, b))
-    quant = timed(lambda: f.quantize_fp8(x))
+    fused = timed(lambda st: f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"]))
+    gemm = timed(lambda st: f.fp8_gemm(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
+    quant = timed(lambda st: f.quantize_fp8(st["x"]))
     pk = peaks()
     # bandwidth-aware roofline for the GEMM: min(tensor peak, AI x HBM)
     ai = wl.flops / wl.gemm_bytes
     roof = min(2.0 * pk["bf16_tflops"], ai * pk["hbm_gbs"] / 1e3)
     g_tf = wl.flops / (gemm * 1e-3) / 1e12
-    return {"workload": name, "M": wl.M, "K": wl.K, "N": wl.N,
+    return {"workload": name, "M": wl.M, "K": wl.K, "N": wl.N, "sets": n_sets,
             "fused_us": round(fused * 1e3, 2),
             "fused_tflops": round(wl.flops / (fused * 1e-3) / 1e12, 1),
             "gemm_us": round(gemm * 1e3, 2), "gemm_tflops": round(g_tf, 1),
@@ -639,7 +679,8 @@ def run_reference(args):
 
 def reference_gpu_timing(wl, args):
     """Device time of the reference's own compiled CUDA ops (cuBLASLt FP8 GEMM + dequant
-    kernel, fp16 out, then the .to(bf16) cast Fp8Linear.forward applies), if built."""
+    kernel, fp16 out, then the .to(bf16) cast Fp8Linear.forward applies), if built,
+    timed like our op: launches back to back over rotating operand sets."""
     try:
         from oracle import build_ref
         ref = build_ref.load()
@@ -651,27 +692,40 @@ def reference_gpu_timing(wl, args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    x = make_x(wl, gen_device="cuda")
-    w, b = make_weight(wl, gen_device="cuda")
-    wq, ws = ref.quantize_weight(w)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    n_sets = set_count(per_set_bytes(wl) + 4 * wl.M * wl.N, dev)  # + its fp32 [M, N] buffer
+    sets = []
+    for i in range(n_sets):
+        x = make_x(wl, seed=7919 * i, gen_device="cuda")
+        w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
+        wq, ws = ref.quantize_weight(w)
+        sets.append({"x": x, "wq": wq, "ws": ws, "b": b})
+        del w
     stream = torch.cuda.current_stream(dev)
-    for _ in range(max(3, args.warmup)):
-        flush.zero_()
-        ref.fp8_linear(x, wq, ws, b).to(x.dtype)
-    torch.cuda.synchronize()
-    evs = []
-    for _ in range(args.steps):
-        flush.zero_()
+
+    def call(st):
+        return ref.fp8_linear(st["x"], st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
+
+    for i in range(max(3, args.warmup)):
+        call(sets[i % n_sets])
+    reps = max(args.steps, n_sets)
+    how = "one CUDA graph"
+    try:
+        g = graph_launches(call, sets, reps, keep=n_sets)
+        ms = time_graph(g, stream, lambda: torch.cuda.synchronize(dev)) / reps
+        del g
+    except Exception:  # pragma: no cover - capture not supported by the library path
+        how = "eager launches (graph capture failed)"
+        torch.cuda.synchronize(dev)
         a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        ref.fp8_linear(x, wq, ws, b).to(x.dtype)
+        for i in range(reps):
+            call(sets[i % n_sets])
         c.record(stream)
-        evs.append((a, c))
-    torch.cuda.synchronize()
-    ms = statistics.mean(a.elapsed_time(c) for a, c in evs)
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(c) / reps
     return {"value": round(wl.flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
             "ms_per_step": round(ms, 4),
+            "timing": f"{reps} steps back to back ({how}) over {n_sets} rotating operand sets",
             "what": "reference fp8_linear (quantize_fp8 + cuBLASLt FP8 GEMM into fp32 + "
                     "dequant_bias_kernel, fp16 out) + .to(bf16), compiled from the "
                     "reference sources for sm_100a"}

@@ -118,6 +118,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::mbar_init(bar_drain, 1);
     *abort = 0;
     ptx::fence_mbar_init();
+    // The weights do not depend on the kernel this one may overlap (PDL): start streaming
+    // them now. The first stages' weight boxes land in shared memory (each stage's barrier
+    // is armed for its weight and token boxes; the token box follows after the dependency
+    // wait), the rest of this CTA's K-range is pulled into L2.
+    const int pre = nkb < STAGES ? nkb : STAGES;
+    for (int i = 0; i < pre; ++i) {
+      const uint32_t fb = bar_full + 8 * i;
+      ptx::mbar_arrive_expect_tx(fb, stage_bytes);
+      ptx::tma_load_2d(sbase + static_cast<uint32_t>(i) * stage_bytes, &tmap_w,
+                       (kb0 + i) * BK, tile * WN, fb);
+    }
+    for (int i = pre; i < nkb; ++i) ptx::tma_prefetch_2d(&tmap_w, (kb0 + i) * BK, tile * WN);
   }
   if (warp == 1) {
     ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t *>(tmem_slot)), p.tmem_cols);
@@ -134,18 +146,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int issued = 0;
       for (int i = 0; i < nkb; ++i) {
         const int s = i % STAGES;
-        const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
-        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kWaitLimitNs)) {
-          if (!*abort) {
-            atomicOr(&g_small_status, 16u);
-            *abort = 1;
-          }
-          break;
-        }
         const uint32_t fb = bar_full + 8 * s;
         const uint32_t dst = sbase + static_cast<uint32_t>(s) * stage_bytes;
-        ptx::mbar_arrive_expect_tx(fb, stage_bytes);
-        ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
+        if (i >= STAGES) {
+          const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
+          if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kWaitLimitNs)) {
+            if (!*abort) {
+              atomicOr(&g_small_status, 16u);
+              *abort = 1;
+            }
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(fb, stage_bytes);
+          ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
+        }  // else: armed and the weight box issued before the dependency wait
         ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, 0, fb);
         ++issued;
       }

@@ -108,6 +108,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int3
       : "memory");
 }
 
+// Brings the box at (x, y) of a tensor into L2 without writing shared memory or
+// signalling any barrier (no cluster multicast). Coordinates follow the load's rules.
+__device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // Same, with an L2 cache-policy hint (a createpolicy value).
 __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void *tmap, int32_t x,
                                                  int32_t y, uint32_t bar, uint64_t policy) {
