@@ -19,6 +19,11 @@
  *   oracle_gemm_dequant     cuBLASLt unscaled e4m3 matmul (csrc/fp8_gemm.cu:109-131,
  *                           180-184) followed by dequant_bias_kernel
  *                           (csrc/fp8_gemm.cu:65-80)
+ *   oracle_mx_sf_offset     the tiled block-scale layout sf_offset (csrc/quantize.cu:75-83)
+ *   oracle_quantize_mxfp8   quant_mxfp8_kernel (csrc/quantize.cu:92-131), launched by
+ *                           quantize_mxfp8 (csrc/quantize.cu:239-285)
+ *   oracle_mxfp8_gemm       cuBLASLt VEC32_UE8M0 block-scaled e4m3 matmul with the bias
+ *                           epilogue, fp16 out (csrc/fp8_gemm.cu:233-340)
  *
  * Arithmetic is IEEE binary32 with round-to-nearest-even and no flush-to-zero,
  * which is what nvcc emits for the reference without --use_fast_math.
@@ -212,6 +217,110 @@ void oracle_gemm_dequant(const uint8_t *xq, const float *xs, const uint8_t *wq,
       if (acc_out) acc_out[m * N + n] = acc;
       volatile float t = acc * xs[m];
       volatile float v = t * ws[n];
+      if (bias16) v = v + oracle_f16_to_f32(bias16[n]);
+      out[m * N + n] = round_out ? oracle_f16_to_f32(oracle_f32_to_f16(v)) : v;
+    }
+  }
+}
+
+/*
+ * Block-scale layout, csrc/quantize.cu:75-83: 512-byte tiles of 128 rows x 4 scale
+ * columns, tiles K-major (column-tile stride 512 B, row-tile stride 512 * ncb B); inside
+ * a tile, scale (r, c) sits at (r % 32) * 16 + ((r % 128) / 32) * 4 + c % 4.
+ */
+int64_t oracle_mx_sf_offset(int64_t r, int64_t c, int64_t ncb) {
+  return (r / 128) * (ncb * 512) + (c / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4);
+}
+
+/* Bytes of the padded scale grid for `rows` rows of K elements (K % 32 == 0). */
+int64_t oracle_mx_sf_bytes(int64_t rows, int64_t K) {
+  return ((rows + 127) / 128) * ((K / 32 + 3) / 4) * 512;
+}
+
+/*
+ * MXFP8 quantization, csrc/quantize.cu:92-131 (one 32-element block of a row):
+ *   amax = fmaxf-reduce |x| over the block (NaN ignored unless the block is all NaN)
+ *   amax > 0 (false for 0 and NaN):
+ *       e8 = clamp(floor(log2(amax)) - 8 + 127, 0, 254), where floor(log2(amax)) is
+ *            the binary exponent of amax (frexpf's exponent - 1). The reference
+ *            evaluates floorf(log2f(amax)); for every bf16 and fp16 amax the two agree
+ *            (pinned against the reference over all of them). An infinite amax takes
+ *            the upper clamp: e8 = 254.
+ *   otherwise e8 = 127
+ *   x_inv = 2^(127 - e8)  (exact power of two)
+ *   q     = e4m3_satfinite(fminf(fmaxf(x * x_inv, -448), 448))
+ * The scale grid (oracle_mx_sf_bytes) is prefilled with 127 (e8m0 1.0) and each block's
+ * e8 written at oracle_mx_sf_offset(row, block, ncb) (csrc/quantize.cu:253-257).
+ */
+void oracle_quantize_mxfp8(const uint16_t *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                           uint8_t *scales) {
+  const int64_t nblk = K / 32, ncb = (nblk + 3) / 4;
+  memset(scales, 127, (size_t)oracle_mx_sf_bytes(M, K));
+  for (int64_t r = 0; r < M; ++r) {
+    for (int64_t g = 0; g < nblk; ++g) {
+      const uint16_t *blk = x + r * K + g * 32;
+      float v[32];
+      float amax = 0.0f;
+      int first = 1;
+      for (int j = 0; j < 32; ++j) {
+        v[j] = dtype ? oracle_f16_to_f32(blk[j]) : oracle_bf16_to_f32(blk[j]);
+        float a = fabsf(v[j]);
+        amax = first ? a : fmaxf(amax, a);
+        first = 0;
+      }
+      int e8;
+      float x_inv;
+      if (amax > 0.0f) {
+        if (isinf(amax)) {
+          e8 = 254;
+        } else {
+          int e2;
+          (void)frexpf(amax, &e2);
+          int ee = (e2 - 1) - 8 + 127;
+          e8 = ee < 0 ? 0 : (ee > 254 ? 254 : ee);
+        }
+        x_inv = ldexpf(1.0f, 127 - e8);
+      } else {
+        e8 = 127;
+        x_inv = 1.0f;
+      }
+      scales[oracle_mx_sf_offset(r, g, ncb)] = (uint8_t)e8;
+      for (int j = 0; j < 32; ++j) {
+        volatile float p = v[j] * x_inv;
+        float c = fminf(fmaxf(p, -E4M3_MAX), E4M3_MAX);
+        xq[r * K + g * 32 + j] = oracle_e4m3_encode(c, 1);
+      }
+    }
+  }
+}
+
+/*
+ * MXFP8 GEMM, csrc/fp8_gemm.cu:233-340: D = A * B with per-32 e8m0 block scales on both
+ * operands, bias epilogue, fp16 out:
+ *   acc[m,n] = sum_k e4m3(xq[m,k]) 2^(xs[m,k/32]-127) * e4m3(wq[n,k]) 2^(ws[n,k/32]-127)
+ *              (each term exact in double; the sum in double, rounded once to fp32)
+ *   out[m,n] = acc + float(bias16[n])  (bias16: the bias rounded to fp16, :257-260)
+ * round_out != 0 rounds out to fp16 (returned widened to fp32). Scale arrays are in
+ * the tiled layout of their operand (rows M for xs, N for ws).
+ */
+void oracle_mxfp8_gemm(const uint8_t *xq, const uint8_t *xs, const uint8_t *wq,
+                       const uint8_t *ws, const uint16_t *bias16, int64_t M, int64_t N,
+                       int64_t K, int round_out, float *out) {
+  float lut[256];
+  for (int i = 0; i < 256; ++i) lut[i] = oracle_e4m3_decode((uint8_t)i);
+  const int64_t nblk = K / 32, ncb = (nblk + 3) / 4;
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      double s = 0.0;
+      for (int64_t g = 0; g < nblk; ++g) {
+        const double sa = ldexp(1.0, (int)xs[oracle_mx_sf_offset(m, g, ncb)] - 127);
+        const double sb = ldexp(1.0, (int)ws[oracle_mx_sf_offset(n, g, ncb)] - 127);
+        double part = 0.0;
+        for (int64_t j = 0; j < 32; ++j)
+          part += (double)lut[xq[m * K + g * 32 + j]] * (double)lut[wq[n * K + g * 32 + j]];
+        s += part * sa * sb;
+      }
+      volatile float v = (float)s;
       if (bias16) v = v + oracle_f16_to_f32(bias16[n]);
       out[m * N + n] = round_out ? oracle_f16_to_f32(oracle_f32_to_f16(v)) : v;
     }

@@ -18,6 +18,8 @@ Reference citations (paths relative to the reference project root):
   weight quant         csrc/quantize.cu:359-365
   GEMM + dequant/bias  csrc/fp8_gemm.cu:139-194, dequant_bias_kernel :65-80
   fused entry          csrc/fp8_gemm.cu:196-221
+  MXFP8 block quant    csrc/quantize.cu:75-131 (layout + kernel), :239-285 (host op)
+  MXFP8 GEMM           csrc/fp8_gemm.cu:233-340 (cuBLASLt VEC32_UE8M0, bias, fp16 out)
 """
 from __future__ import annotations
 
@@ -76,6 +78,12 @@ def lib() -> ctypes.CDLL:
         L.oracle_gemm_dequant.restype = None
         L.oracle_f32_to_f16.argtypes = [ctypes.c_float]
         L.oracle_f32_to_f16.restype = ctypes.c_uint16
+        L.oracle_mx_sf_bytes.argtypes = [i64, i64]
+        L.oracle_mx_sf_bytes.restype = i64
+        L.oracle_quantize_mxfp8.argtypes = [P, ctypes.c_int, i64, i64, P, P]
+        L.oracle_quantize_mxfp8.restype = None
+        L.oracle_mxfp8_gemm.argtypes = [P, P, P, P, P, i64, i64, i64, ctypes.c_int, P]
+        L.oracle_mxfp8_gemm.restype = None
         _lib = L
     return _lib
 
@@ -121,6 +129,42 @@ def c_gemm_dequant(xq, xs, wq, ws, bias16=None, round_out=True, want_acc=False):
     lib().oracle_gemm_dequant(_ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws), _ptr(bias16),
                               M, N, K, int(round_out), _ptr(acc), _ptr(out))
     return (out, acc) if want_acc else out
+
+
+def mx_sf_bytes(rows: int, K: int) -> int:
+    """Bytes of the padded MXFP8 scale grid: ceil(rows/128) * ceil((K/32)/4) * 512."""
+    return ((rows + 127) // 128) * ((K // 32 + 3) // 4) * 512
+
+
+def mx_sf_offset(r, c, ncb):
+    """Offset of block scale (row r, block c) in the tiled layout (csrc/quantize.cu:80-83);
+    works elementwise on numpy integer arrays."""
+    return (r // 128) * (ncb * 512) + (c // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + (c % 4)
+
+
+def c_quantize_mxfp8(x16: np.ndarray, dtype: int = BF16):
+    """MXFP8 codes [M, K] and the tiled e8m0 scale grid (1-D uint8)."""
+    x16 = np.ascontiguousarray(x16, dtype=np.uint16)
+    M, K = x16.shape
+    xq = np.empty((M, K), np.uint8)
+    sc = np.empty((mx_sf_bytes(M, K),), np.uint8)
+    lib().oracle_quantize_mxfp8(_ptr(x16), dtype, M, K, _ptr(xq), _ptr(sc))
+    return xq, sc
+
+
+def c_mxfp8_gemm(xq, xs, wq, ws, bias16=None, round_out=True):
+    xq = np.ascontiguousarray(xq, np.uint8)
+    wq = np.ascontiguousarray(wq, np.uint8)
+    xs = np.ascontiguousarray(xs, np.uint8)
+    ws = np.ascontiguousarray(ws, np.uint8)
+    if bias16 is not None:
+        bias16 = np.ascontiguousarray(bias16, np.uint16)
+    M, K = xq.shape
+    N = wq.shape[0]
+    out = np.empty((M, N), np.float32)
+    lib().oracle_mxfp8_gemm(_ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws), _ptr(bias16), M, N, K,
+                            int(round_out), _ptr(out))
+    return out
 
 
 def c_e4m3_encode(v: float, saturate: bool = True) -> int:
@@ -287,3 +331,63 @@ def norm_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
+
+
+# ----------------------------------------------------------------------------- MXFP8 numpy twins
+
+
+def np_mx_block_exponent(amax: np.ndarray) -> np.ndarray:
+    """e8m0 block scale from block amax (float32 array), the rule of
+    oracle_quantize_mxfp8: clamp(exponent(amax) - 8 + 127, 0, 254) for amax > 0
+    (254 for inf), 127 for zero and NaN."""
+    a = np.asarray(amax, np.float32)
+    with np.errstate(invalid="ignore"):
+        _, e2 = np.frexp(np.where(np.isfinite(a) & (a > 0), a, np.float32(1.0)))
+    e8 = np.clip(e2.astype(np.int64) - 1 - 8 + 127, 0, 254)
+    e8 = np.where(np.isinf(a), 254, e8)
+    with np.errstate(invalid="ignore"):
+        pos = a > 0
+    return np.where(pos, e8, 127).astype(np.uint8)
+
+
+def np_quantize_mxfp8(x16: np.ndarray, dtype: int = BF16):
+    """Vectorised twin of c_quantize_mxfp8."""
+    x16 = np.ascontiguousarray(x16, dtype=np.uint16)
+    M, K = x16.shape
+    nblk, ncb = K // 32, (K // 32 + 3) // 4
+    x = bf16_bits_to_f32(x16) if dtype == BF16 else f16_bits_to_f32(x16)
+    blk = np.abs(x.reshape(M, nblk, 32))
+    all_nan = np.all(np.isnan(blk), axis=2)
+    amax = np.max(np.where(np.isnan(blk), np.float32(-1.0), blk), axis=2)
+    amax = np.where(all_nan, np.float32(np.nan), amax).astype(np.float32)
+    e8 = np_mx_block_exponent(amax)
+    inv = np.ldexp(np.float32(1.0), (127 - e8.astype(np.int32))).astype(np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        p = (x.reshape(M, nblk, 32) * inv[:, :, None]).astype(np.float32)
+    c = np.minimum(np.maximum(p, -E4M3_MAX), E4M3_MAX)  # numpy max/min propagate NaN
+    c = np.where(np.isnan(p), -E4M3_MAX, c)             # fminf(fmaxf(NaN, -448), 448) = -448
+    xq = np_e4m3_encode(c.reshape(M, K), saturate=True)
+    sc = np.full((mx_sf_bytes(M, K),), 127, np.uint8)
+    r, g = np.meshgrid(np.arange(M), np.arange(nblk), indexing="ij")
+    sc[mx_sf_offset(r, g, ncb)] = e8
+    return xq, sc
+
+
+def np_mx_decode(q: np.ndarray, sc: np.ndarray) -> np.ndarray:
+    """float64 values of MXFP8 codes [R, K] with their tiled scale grid."""
+    R, K = q.shape
+    nblk, ncb = K // 32, (K // 32 + 3) // 4
+    r, g = np.meshgrid(np.arange(R), np.arange(nblk), indexing="ij")
+    e8 = sc[mx_sf_offset(r, g, ncb)].astype(np.int64)
+    dec = e4m3_decode_lut().astype(np.float64)[q].reshape(R, nblk, 32)
+    return (dec * np.ldexp(1.0, e8 - 127)[:, :, None]).reshape(R, K)
+
+
+def np_mxfp8_gemm(xq, xs, wq, ws, bias16=None, round_out=False):
+    """Decoded float64 matmul (twin of c_mxfp8_gemm up to summation order)."""
+    acc = (np_mx_decode(xq, xs) @ np_mx_decode(wq, ws).T).astype(np.float32)
+    if bias16 is not None:
+        acc = acc + f16_bits_to_f32(np.asarray(bias16, np.uint16))[None, :]
+    if round_out:
+        acc = acc.astype(np.float16).astype(np.float32)
+    return acc
