@@ -26,6 +26,8 @@ SIGNATURES = {
     "fp8lin_last_error": (ctypes.c_char_p, []),
     "fp8lin_quantize_fp8": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
     "fp8lin_quantize_weight": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
+    "fp8lin_mx_scale_bytes": (_SZ, [_I64, _I64]),
+    "fp8lin_quantize_mxfp8": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
     "fp8lin_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
     "fp8lin_linear_workspace_size": (_SZ, [_I64, _I64]),
     "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
@@ -74,6 +76,20 @@ class CApi:
                                           scale.data_ptr(), self._stream(x))
         self._check(rc, "fp8lin_quantize_fp8")
         return xq, scale
+
+    def mx_scale_bytes(self, rows: int, K: int) -> int:
+        return int(self.lib.fp8lin_mx_scale_bytes(rows, K))
+
+    def quantize_mxfp8(self, x: torch.Tensor, xq: torch.Tensor | None = None,
+                       scales: torch.Tensor | None = None):
+        M, K = x.shape
+        xq = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device) if xq is None else xq
+        if scales is None:
+            scales = torch.empty((self.mx_scale_bytes(M, K),), dtype=torch.uint8, device=x.device)
+        rc = self.lib.fp8lin_quantize_mxfp8(x.data_ptr(), DTYPE[x.dtype], M, K, xq.data_ptr(),
+                                            scales.data_ptr(), self._stream(x))
+        self._check(rc, "fp8lin_quantize_mxfp8")
+        return xq, scales
 
     def quantize_weight(self, w: torch.Tensor):
         N, K = w.shape

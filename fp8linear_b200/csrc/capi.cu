@@ -120,6 +120,36 @@ int fp8lin_quantize_fp8(const void *x, int x_dtype, int64_t M, int64_t K, void *
   return FP8LIN_OK;
 }
 
+size_t fp8lin_mx_scale_bytes(int64_t rows, int64_t K) {
+  if (rows <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(mx_scale_bytes(rows, K));
+}
+
+int fp8lin_quantize_mxfp8(const void *x, int x_dtype, int64_t M, int64_t K, void *xq,
+                          void *scales, void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_mxfp8: x must be fp16 or bf16");
+  if (M < 0 || K < 0) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_mxfp8: negative size");
+  if (K % 32 != 0)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                "quantize_mxfp8: K must be a multiple of 32 for MXFP8, got " + std::to_string(K));
+  if (M == 0) return FP8LIN_OK;
+  if (K == 0) return fail(FP8LIN_ERR_UNSUPPORTED, "quantize_mxfp8: K must be positive");
+  if (!x || !xq || !scales)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_mxfp8: null pointer");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(xq) % 8 ||
+      reinterpret_cast<uintptr_t>(scales) % 4)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                "quantize_mxfp8: x must be 16-byte, xq 8-byte and scales 4-byte aligned");
+  cudaError_t e = launch_quantize_mx(x, x_dtype, M, K, static_cast<uint8_t *>(xq),
+                                     static_cast<uint8_t *>(scales),
+                                     static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("quantize_mxfp8: launch: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
 int fp8lin_quantize_weight(const void *w, int w_dtype, int64_t N, int64_t K, void *wq,
                            float *w_scale, void *stream) {
   clear_error();

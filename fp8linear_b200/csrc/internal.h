@@ -33,6 +33,14 @@ bool current_device_info(DeviceInfo *info);
 // Per-token quantization (activation path). Returns cudaSuccess or the launch error.
 cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
                                  float *scale, cudaStream_t stream, bool trigger_dependents);
+// MXFP8 block quantization (per 32 elements along K, e8m0 scales in the tiled
+// block-scale layout; the whole padded scale grid of mx_scale_bytes(M, K) is written).
+// K % 32 == 0, x 16-byte aligned, xq 8-byte aligned, scales 4-byte aligned.
+cudaError_t launch_quantize_mx(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                               uint8_t *scales, cudaStream_t stream, bool trigger_dependents);
+inline int64_t mx_scale_bytes(int64_t rows, int64_t K) {
+  return (rows + 127) / 128 * ((K / 32 + 3) / 4) * 512;
+}
 // Reads (and optionally clears) the quantizer watchdog bits (8) of the current device.
 cudaError_t read_quant_status(unsigned int *bits, bool clear);
 // Per-channel weight quantization (ATen semantics of the reference's quantize_weight).

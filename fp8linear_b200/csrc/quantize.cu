@@ -538,6 +538,137 @@ cudaError_t launch_rows_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, 
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- MXFP8 block quantizer
+//
+// Replaces quant_mxfp8_kernel (csrc/quantize.cu:92-131 of the reference): per 32-element
+// block of a row, a power-of-two (e8m0) scale and e4m3 codes, the scales written in
+// the tiled block-scale layout the block-scaled tensor-core GEMM reads (512-byte tiles
+// of 128 rows x 4 scale columns; scale (r, c) at tile (r / 128, c / 4), byte
+// (r % 32) * 16 + ((r % 128) / 32) * 4 + c % 4; tiles ordered K-major).
+//   amax  = max |x| over the block, NaN ignored (an all-NaN block counts as 0)
+//   e8    = 127 for amax 0; 254 for an infinite amax; otherwise
+//           clamp(exponent(amax) + 119, 0, 254) with exponent(amax) = floor(log2(amax)),
+//           read exactly from the magnitude's bits (the reference's floorf(log2f(amax))
+//           agrees with it for every bf16 and fp16 amax)
+//   q     = e4m3_satfinite(fminf(fmaxf(x * 2^(127 - e8), -448), 448))
+// One warp owns a 1024-element segment of a row: lane l holds elements (32 i + l) * 8 ..
+// +7 of vector i (i = 0..3), so each block is 4 consecutive lanes (amax by two
+// shuffles) and each 4-block group of scales (4 consecutive bytes of the layout) is one
+// 32-bit store by lane 0 or 16. Warps past row M, and blocks past K/32 inside the last
+// 4-block group of a row, write the padding value 127 (e8m0 1.0), so the whole padded
+// grid is written and needs no prefill.
+template <typename T>
+struct MxBits;
+template <>
+struct MxBits<__nv_bfloat16> {
+  static constexpr uint32_t kInf = 0x7F80u;
+  // floor(log2(value)) of a nonzero finite magnitude bit pattern
+  __device__ __forceinline__ static int exponent(uint32_t mag) {
+    const uint32_t f = mag >> 7;
+    return f ? static_cast<int>(f) - 127 : (31 - __clz(static_cast<int>(mag & 0x7Fu))) - 133;
+  }
+};
+template <>
+struct MxBits<__half> {
+  static constexpr uint32_t kInf = 0x7C00u;
+  __device__ __forceinline__ static int exponent(uint32_t mag) {
+    const uint32_t f = mag >> 10;
+    return f ? static_cast<int>(f) - 15 : (31 - __clz(static_cast<int>(mag & 0x3FFu))) - 24;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ uint32_t mx_mag_max8(const uint4 &v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t mx = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = w[i] & 0x7FFFu, hi = (w[i] >> 16) & 0x7FFFu;
+    mx = max(mx, lo > MxBits<T>::kInf ? 0u : lo);  // NaN patterns count as 0
+    mx = max(mx, hi > MxBits<T>::kInf ? 0u : hi);
+  }
+  return mx;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t mx_block_e8(uint32_t mag) {
+  if (mag == 0) return 127u;
+  if (mag == MxBits<T>::kInf) return 254u;
+  const int e8 = MxBits<T>::exponent(mag) + 119;
+  return static_cast<uint32_t>(e8 < 0 ? 0 : (e8 > 254 ? 254 : e8));
+}
+
+// 2^(127 - e8) for e8 in 0..254, exactly (2^-127 is a subnormal float)
+__device__ __forceinline__ float mx_inv(uint32_t e8) {
+  const int e = 127 - static_cast<int>(e8);
+  return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
+                   : __uint_as_float(0x00400000u);
+}
+
+constexpr int kMxWarps = 8;
+constexpr int kMxVecs = 4;                       // 16-byte vectors per lane
+constexpr int kMxSeg = 32 * kMxVecs * 8;         // elements per warp segment (1024)
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kMxWarps) quant_mx_kernel(
+    const T *__restrict__ x, uint8_t *__restrict__ xq, uint8_t *__restrict__ sf, int64_t M,
+    int K, int64_t rows_pad, int segs, int ncb, int trigger) {
+  if (trigger) ptx::grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * kMxWarps + (threadIdx.x >> 5);
+  const int64_t row = wid / segs;
+  if (row >= rows_pad) return;  // warp-uniform
+  const int seg = static_cast<int>(wid - row * segs);
+  const int nblk = K >> 5;
+  const bool row_live = row < M;
+  const int e0 = seg * kMxSeg;
+  const T *xr = x + (row_live ? row : 0) * static_cast<int64_t>(K);
+  uint4 v[kMxVecs];
+#pragma unroll
+  for (int i = 0; i < kMxVecs; ++i) {
+    const int el = e0 + (i * 32 + lane) * 8;
+    v[i] = (row_live && el < K) ? ld_stream_v4(xr + el) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  const int64_t sf_row = (row >> 7) * static_cast<int64_t>(ncb) * 512 + (row & 31) * 16 +
+                         ((row & 127) >> 5) * 4;
+#pragma unroll
+  for (int i = 0; i < kMxVecs; ++i) {
+    const int el = e0 + (i * 32 + lane) * 8;
+    const int g = el >> 5;  // this lane's block
+    const bool live = row_live && g < nblk;
+    uint32_t mag = live ? mx_mag_max8<T>(v[i]) : 0u;
+    mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 1));
+    mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 2));
+    const uint32_t e8 = live ? mx_block_e8<T>(mag) : 127u;
+    // the scales of blocks g .. g+3 from lanes l, l+4, l+8, l+12 (l = 0, 16)
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, e8, 4);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, e8, 8);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, e8, 12);
+    const int grp = g >> 2;
+    if ((lane & 15) == 0 && grp < ncb)
+      *reinterpret_cast<uint32_t *>(sf + sf_row + static_cast<int64_t>(grp) * 512) =
+          e8 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (live)
+      *reinterpret_cast<uint2 *>(xq + row * static_cast<int64_t>(K) + el) =
+          quant8_clamp<T>(v[i], mx_inv(e8));
+  }
+}
+
+template <typename T>
+cudaError_t launch_mx_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, uint8_t *sf,
+                            cudaStream_t stream, bool trigger) {
+  const int64_t rows_pad = (M + 127) / 128 * 128;
+  const int segs = static_cast<int>((K + kMxSeg - 1) / kMxSeg);
+  const int ncb = static_cast<int>((K / 32 + 3) / 4);
+  const int64_t warps = rows_pad * segs;
+  const int64_t blocks = (warps + kMxWarps - 1) / kMxWarps;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  quant_mx_kernel<T><<<static_cast<unsigned>(blocks), 32 * kMxWarps, 0, stream>>>(
+      reinterpret_cast<const T *>(x), xq, sf, M, static_cast<int>(K), rows_pad, segs, ncb,
+      trigger ? 1 : 0);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
@@ -546,6 +677,14 @@ cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K,
   if (dtype == kBF16)
     return launch_rows_typed<__nv_bfloat16>(x, M, K, xq, scale, stream, trigger_dependents);
   return launch_rows_typed<__half>(x, M, K, xq, scale, stream, trigger_dependents);
+}
+
+cudaError_t launch_quantize_mx(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                               uint8_t *scales, cudaStream_t stream, bool trigger_dependents) {
+  if (M == 0) return cudaSuccess;
+  if (dtype == kBF16)
+    return launch_mx_typed<__nv_bfloat16>(x, M, K, xq, scales, stream, trigger_dependents);
+  return launch_mx_typed<__half>(x, M, K, xq, scales, stream, trigger_dependents);
 }
 
 cudaError_t read_quant_status(unsigned int *bits, bool clear) {

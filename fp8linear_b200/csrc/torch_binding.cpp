@@ -12,8 +12,9 @@
 // (csrc/fp8_gemm.cu:163). Here fp8_linear returns x's dtype (bf16 for bf16 input,
 // fp16 for fp16 input) and fp8_gemm returns bf16.
 //
-// The reference's MXFP8 / NVFP4 schemas (torch-ext/torch_binding.cpp:30-65) are
-// registered so that code probing for them finds them, and raise a clear error.
+// The reference's MXFP8 schemas (torch-ext/torch_binding.cpp:30-46): quantize_mxfp8 is
+// implemented; its NVFP4 schemas (:48-65) are registered so that code probing for them
+// finds them, and raise a clear error.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
@@ -187,7 +188,29 @@ at::Tensor fp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scale,
               "(quantize_fp8 / quantize_weight / fp8_gemm / fp8_linear) is implemented");
 }
 
-std::tuple<at::Tensor, at::Tensor> quantize_mxfp8(at::Tensor) { unsupported("quantize_mxfp8"); }
+// quantize_mxfp8 (csrc/quantize.cu:239-285): same checks and outputs; the scale grid is
+// written whole by the kernel (padding included), so it is allocated uninitialised
+// instead of being prefilled with 127 as the reference does.
+std::tuple<at::Tensor, at::Tensor> quantize_mxfp8(at::Tensor x) {
+  TORCH_CHECK(x.is_cuda(), "x must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
+              "x must be fp16 or bf16");
+  TORCH_CHECK(x.dim() == 2, "x must be 2D [M, K]");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto xc = aligned16(x);
+  const int64_t M = xc.size(0), K = xc.size(1);
+  TORCH_CHECK(K % 32 == 0, "K must be a multiple of 32 for MXFP8, got ", K);
+  auto xq = at::empty_like(xc, xc.options().dtype(at::kFloat8_e4m3fn));
+  const int64_t sf_bytes = (M + 127) / 128 * ((K / 32 + 3) / 4) * 512;
+  if (M == 0 || K == 0) {
+    return {xq, at::full({sf_bytes}, 127, xc.options().dtype(at::kByte))};
+  }
+  auto scales = at::empty({sf_bytes}, xc.options().dtype(at::kByte));
+  check_rc(fp8lin_quantize_mxfp8(xc.data_ptr(), dtype_code(xc.scalar_type()), M, K,
+                                 xq.data_ptr(), scales.data_ptr(), stream_of(xc)),
+           "quantize_mxfp8");
+  return {xq, scales};
+}
 at::Tensor mxfp8_gemm(at::Tensor, at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
   unsupported("mxfp8_gemm");
 }

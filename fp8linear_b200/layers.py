@@ -11,7 +11,8 @@ Same public names and contracts:
 
 Differences from the reference: ``fp8_linear`` returns ``x.dtype`` (the reference
 returns fp16 and ``Fp8Linear.forward`` casts back); ``fp8_gemm`` returns bf16; the
-MXFP8 / NVFP4 entry points exist but raise ``NotImplementedError``.
+MXFP8 quantizer (``quantize_mxfp8`` / ``quantize_weight_mxfp8``) is implemented; the
+remaining MXFP8 / NVFP4 entry points exist but raise ``NotImplementedError``.
 """
 from __future__ import annotations
 
@@ -47,6 +48,22 @@ def _fp8_gemm_fake(xq, x_scale, wq, w_scale, bias=None):
     return xq.new_empty((xq.shape[0], wq.shape[0]), dtype=torch.bfloat16)
 
 
+MX_BLOCK = 32
+
+
+def mx_scale_bytes(rows: int, K: int) -> int:
+    """Bytes of the MXFP8 block-scale grid: 512-byte tiles over ceil(rows/128) x
+    ceil((K/32)/4) (layers.py:33-36 of the reference)."""
+    return ((rows + 127) // 128) * ((K // MX_BLOCK + 3) // 4) * 512
+
+
+@torch.library.register_fake(add_op_namespace_prefix("quantize_mxfp8"))
+def _quantize_mxfp8_fake(x):
+    xq = x.new_empty(x.shape, dtype=torch.float8_e4m3fn)
+    scales = x.new_empty((mx_scale_bytes(x.shape[0], x.shape[1]),), dtype=torch.uint8)
+    return xq, scales
+
+
 def _not_provided(name: str):
     raise NotImplementedError(
         f"{name}: fp8linear_b200 implements the per-channel FP8 path only "
@@ -55,8 +72,14 @@ def _not_provided(name: str):
 
 
 def quantize_weight_mxfp8(weight: torch.Tensor):
-    """Not provided (the reference's opt-in MXFP8 format); raises NotImplementedError."""
-    _not_provided("quantize_weight_mxfp8")
+    """MXFP8 block quantization of a ``[N, K]`` weight (offline; layers.py:72-81 of the
+    reference): ``(wq e4m3 [N, K], scales uint8)`` with one e8m0 scale per 32 weights
+    along K, in the tiled block-scale layout the block-scaled GEMM reads. fp32 weights
+    are cast to bf16 first, as the reference does."""
+    w = weight.detach()
+    if w.dtype not in (torch.float16, torch.bfloat16):
+        w = w.to(torch.bfloat16)
+    return ops.quantize_mxfp8(w.contiguous())
 
 
 def mxfp8_linear(x, wq, w_scales, bias=None):

@@ -69,6 +69,29 @@ FP8LIN_API int fp8lin_quantize_fp8(const void *x, int x_dtype, int64_t M, int64_
                                    void *xq, float *x_scale, void *stream);
 
 /*
+ * Bytes of the MXFP8 block-scale grid for `rows` rows of K elements (K % 32 == 0):
+ * ceil(rows / 128) * ceil((K / 32) / 4) * 512, the padded tile grid of
+ * csrc/quantize.cu:244-250 (quantize_mxfp8's scales tensor size).
+ */
+FP8LIN_API size_t fp8lin_mx_scale_bytes(int64_t rows, int64_t K);
+
+/*
+ * MXFP8 block quantization (OCP microscaling: e4m3 codes, one power-of-two e8m0 scale per
+ * 32 elements along K).
+ * Replaces quantize_mxfp8 (csrc/quantize.cu:239-285; kernel csrc/quantize.cu:92-131);
+ * applies to activations and, offline, to weights (quantize_weight_mxfp8).
+ *   x      [M, K] row-major, x_dtype BF16 or F16, K % 32 == 0, 16-byte aligned
+ *   xq     [M, K] e4m3fn codes, 8-byte aligned
+ *   scales fp8lin_mx_scale_bytes(M, K) bytes, 4-byte aligned: the e8m0 scale of block
+ *          (r, c) at (r/128)*ncb*512 + (c/4)*512 + (r%32)*16 + ((r%128)/32)*4 + c%4,
+ *          ncb = ceil((K/32)/4) (csrc/quantize.cu:75-83); padding entries are written
+ *          with 127 (scale 1.0), so the buffer needs no prefill.
+ * Codes and scales are bit-identical to the reference kernel. M == 0 is a no-op.
+ */
+FP8LIN_API int fp8lin_quantize_mxfp8(const void *x, int x_dtype, int64_t M, int64_t K,
+                                     void *xq, void *scales, void *stream);
+
+/*
  * Per-output-channel e4m3 weight quantization (offline, once per weight).
  * Replaces the per-channel branch of quantize_weight (csrc/quantize.cu:341-366),
  * which the reference evaluates with ATen ops on the GPU:

@@ -108,7 +108,5 @@ def test_linear_rejects_block_scaled_formats():
     wq = torch.zeros(16, 64, dtype=torch.float8_e4m3fn, device="cuda")
     with pytest.raises(RuntimeError, match="not supported"):
         f.fp8_linear(x, wq, torch.zeros(512, dtype=torch.uint8, device="cuda"), None)
-    with pytest.raises(RuntimeError, match="not provided"):
-        f.quantize_mxfp8(x)
     with pytest.raises(NotImplementedError):
         f.quantize_weight_nvfp4(x)

@@ -63,7 +63,8 @@ def test_cpu_tensors_fail_loudly():
 
 
 def test_block_scaled_entry_points_raise():
-    with pytest.raises(NotImplementedError):
+    # the MXFP8 quantizer exists but, like every op here, has no CPU kernel
+    with pytest.raises((RuntimeError, NotImplementedError)):
         f.quantize_weight_mxfp8(torch.zeros(4, 32))
     with pytest.raises(NotImplementedError):
         f.mxfp8_linear(None, None, None)
