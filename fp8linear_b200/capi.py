@@ -28,6 +28,9 @@ SIGNATURES = {
     "fp8lin_quantize_weight": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
     "fp8lin_mx_scale_bytes": (_SZ, [_I64, _I64]),
     "fp8lin_quantize_mxfp8": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
+    "fp8lin_mxfp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
+    "fp8lin_mxfp8_linear_workspace_size": (_SZ, [_I64, _I64]),
+    "fp8lin_mxfp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
     "fp8lin_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
     "fp8lin_linear_workspace_size": (_SZ, [_I64, _I64]),
     "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
@@ -66,6 +69,14 @@ class CApi:
         dev = t.device if t is not None else torch.device("cuda")
         return torch.cuda.current_stream(dev).cuda_stream
 
+    @staticmethod
+    def _bias_ptr(bias):
+        return None if bias is None else bias.data_ptr()
+
+    @staticmethod
+    def _bias_dtype(bias):
+        return DTYPE_NONE if bias is None else DTYPE[bias.dtype]
+
     # -- entry points
     def quantize_fp8(self, x: torch.Tensor, xq: torch.Tensor | None = None,
                      scale: torch.Tensor | None = None):
@@ -90,6 +101,33 @@ class CApi:
                                             scales.data_ptr(), self._stream(x))
         self._check(rc, "fp8lin_quantize_mxfp8")
         return xq, scales
+
+    def mxfp8_gemm(self, xq, x_scales, wq, w_scales, bias=None, out_dtype=torch.bfloat16,
+                   out=None):
+        M, K = xq.shape
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=out_dtype, device=xq.device) if out is None else out
+        rc = self.lib.fp8lin_mxfp8_gemm(xq.data_ptr(), x_scales.data_ptr(), wq.data_ptr(),
+                                        w_scales.data_ptr(), self._bias_ptr(bias),
+                                        self._bias_dtype(bias), out.data_ptr(), DTYPE[out.dtype],
+                                        M, N, K, self._stream(xq))
+        self._check(rc, "fp8lin_mxfp8_gemm")
+        return out
+
+    def mxfp8_linear(self, x, wq, w_scales, bias=None, out=None, workspace=None):
+        M, K = x.shape
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device) if out is None else out
+        need = int(self.lib.fp8lin_mxfp8_linear_workspace_size(M, K))
+        if workspace is None:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+        rc = self.lib.fp8lin_mxfp8_linear(x.data_ptr(), DTYPE[x.dtype], wq.data_ptr(),
+                                          w_scales.data_ptr(), self._bias_ptr(bias),
+                                          self._bias_dtype(bias), out.data_ptr(),
+                                          DTYPE[out.dtype], M, N, K, workspace.data_ptr(),
+                                          workspace.numel(), self._stream(x))
+        self._check(rc, "fp8lin_mxfp8_linear")
+        return out
 
     def quantize_weight(self, w: torch.Tensor):
         N, K = w.shape

@@ -64,27 +64,46 @@ constexpr uint32_t EPI_BUF = 32 * EPI_COLS * 2;  // 4 KB: 32 rows x 64 cols x 2 
 constexpr uint32_t PAR_BYTES = 2 * BN * 4;       // per epilogue warp: w_scale + bias of a tile
 constexpr uint32_t RING_BYTES = 160 * 1024;      // operand ring (both shapes)
 
-template <int CG>
+// MX = true: the MXFP8 (block-scaled) form. Each stage also carries the e8m0 scale tiles
+// of the K-block: one 512-byte tile for this CTA's 128 rows of A and two for the tile's
+// 256 rows of B (every CTA of a pair holds the scales of all 256 B rows, which the MMA
+// reads for its N = 256). Before a K-block's MMAs they are copied into TMEM
+// (tcgen05.cp .32x128b.warpx4, 4 columns per tile) next to the accumulators. To make room,
+// the two accumulators overlap by one epilogue chunk: accumulator 0 = columns 0-255,
+// accumulator 1 = columns 192-447, scale factors at 448-459; the epilogue reads the shared
+// chunk first and releases it before the rest (bar_tovl).
+template <int CG, bool MX = false>
 struct Cfg {
   static constexpr int B_ROWS = BN / CG;                       // B rows this CTA loads
   static constexpr uint32_t B_STAGE = B_ROWS * BK;             // 32 KB (CG 1) / 16 KB (CG 2)
-  static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
-  static constexpr int STAGES = RING_BYTES / STAGE;            // 3 / 5
+  static constexpr uint32_t SFA_STAGE = MX ? 512u : 0u;        // A scales of the K-block
+  static constexpr uint32_t SFB_STAGE = MX ? 1024u : 0u;       // B scales, all 256 rows
+  static constexpr uint32_t STAGE = A_STAGE + B_STAGE + SFA_STAGE + SFB_STAGE;
+  static constexpr uint32_t RING = MX ? 168u * 1024u : RING_BYTES;
+  static constexpr int STAGES = RING / STAGE;                  // 3 / 5 (MX: 3 / 5)
   static constexpr uint32_t TX_BYTES = CG * STAGE;             // bytes landing per stage
   static constexpr int TILE_M = BM * CG;
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_B = OFF_A + STAGES * A_STAGE;
-  static constexpr uint32_t OFF_EPI = OFF_B + STAGES * B_STAGE;
+  static constexpr uint32_t OFF_SFA = OFF_B + STAGES * B_STAGE;
+  static constexpr uint32_t OFF_SFB = OFF_SFA + STAGES * SFA_STAGE;
+  static constexpr uint32_t OFF_EPI = (OFF_SFB + STAGES * SFB_STAGE + 1023u) & ~1023u;
   static constexpr uint32_t OFF_PAR = OFF_EPI + EPI_WARPS * 2 * EPI_BUF;
   static constexpr uint32_t OFF_BAR = OFF_PAR + EPI_WARPS * PAR_BYTES;
-  static constexpr uint32_t NUM_BARS = 2 * STAGES + 5;  // full, empty, tfull x2, tempty x2, drain
+  // full, empty, tfull x2, tempty x2, drain, overlap-chunk release (MX)
+  static constexpr uint32_t NUM_BARS = 2 * STAGES + 6;
   static constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
   static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
   static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + base alignment slack
   static constexpr uint32_t IDESC = ptx::idesc_e4m3_f32(TILE_M, BN);
-  static_assert(STAGES * STAGE <= RING_BYTES, "ring");
+  static constexpr uint32_t IDESC_MX = ptx::idesc_mx_e4m3(TILE_M, BN, 0);
+  static constexpr uint32_t ACC1_COL = MX ? BN - EPI_COLS : BN;  // accumulator 1's column
+  static constexpr uint32_t SFA_COL = 2 * BN - EPI_COLS;          // MX scale factors
+  static constexpr uint32_t SFB_COL = SFA_COL + 4;
+  static_assert(STAGES * STAGE <= RING, "ring");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(OFF_B % 1024 == 0 && OFF_EPI % 1024 == 0, "swizzle atoms need 1024 B alignment");
+  static_assert(!MX || SFB_COL + 8 <= TMEM_COLS, "TMEM budget");
 };
 
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
@@ -98,6 +117,7 @@ struct Params {
   int out_dtype;
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
+  int ncb;           // MX: scale tiles per 128-row block (ceil(K / 128))
   int n_fastest;     // tile order
   int direct_store;  // rows not 16-byte multiples / unaligned: no TMA store
   void *out;         // output base (direct stores)
@@ -134,12 +154,14 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
   }
 }
 
-template <int CG>
+template <int CG, bool MX>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
-                    const __grid_constant__ CUtensorMap tmap_out, const Params p) {
-  using C = Cfg<CG>;
+                    const __grid_constant__ CUtensorMap tmap_out,
+                    const __grid_constant__ CUtensorMap tmap_sfa,
+                    const __grid_constant__ CUtensorMap tmap_sfb, const Params p) {
+  using C = Cfg<CG, MX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -149,6 +171,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t bar_tfull = bar_empty + C::STAGES * 8;    // 2 barriers
   const uint32_t bar_tempty = bar_tfull + 2 * 8;           // 2 barriers
   const uint32_t bar_drain = bar_tempty + 2 * 8;           // MMA drain on the way out
+  const uint32_t bar_tovl = bar_drain + 8;                 // MX: overlap chunk read
   volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + C::OFF_TMEM_SLOT);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + C::OFF_ABORT);
 
@@ -163,6 +186,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
     ptx::prefetch_tmap(&tmap_out);
+    if constexpr (MX) {
+      ptx::prefetch_tmap(&tmap_sfa);
+      ptx::prefetch_tmap(&tmap_sfb);
+    }
     for (int s = 0; s < C::STAGES; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
       ptx::mbar_init(bar_empty + 8 * s, 1);
@@ -172,6 +199,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_init(bar_tempty + 8 * a, EPI_WARPS * CG);
     }
     ptx::mbar_init(bar_drain, 1);
+    ptx::mbar_init(bar_tovl, EPI_WARPS * CG);
     *abort = 0;
     ptx::fence_mbar_init();
   }
@@ -212,16 +240,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = bar_full + 8 * stage;
           const uint32_t dst_a = sbase + C::OFF_A + stage * A_STAGE;
           const uint32_t dst_b = sbase + C::OFF_B + stage * C::B_STAGE;
+          // MX scale tiles of this K-block: row (128-row block * ncb + kb) of the tiled
+          // scale arrays; blocks past the end read as zero (rows that are never stored).
+          const int sfa_row = (a_row >> 7) * p.ncb + kb;
+          const int sfb_row = ((nt * BN) >> 7) * p.ncb + kb;
+          const uint32_t dst_sfa = sbase + C::OFF_SFA + stage * C::SFA_STAGE;
+          const uint32_t dst_sfb = sbase + C::OFF_SFB + stage * C::SFB_STAGE;
           if constexpr (CG == 1) {
             ptx::mbar_arrive_expect_tx(fb, C::TX_BYTES);
             ptx::tma_load_2d(dst_a, &tmap_a, kb * BK, a_row, fb);
             ptx::tma_load_2d(dst_b, &tmap_b, kb * BK, b_row, fb);
+            if constexpr (MX) {
+              ptx::tma_load_2d(dst_sfa, &tmap_sfa, 0, sfa_row, fb);
+              ptx::tma_load_2d(dst_sfb, &tmap_sfb, 0, sfb_row, fb);
+              ptx::tma_load_2d(dst_sfb + 512, &tmap_sfb, 0, sfb_row + p.ncb, fb);
+            }
           } else {
             // Both CTAs' bytes complete the leader's barrier; only the leader arms it.
             if (leader) ptx::mbar_arrive_expect_tx(fb, C::TX_BYTES);
             const uint32_t fb_leader = ptx::map_shared_rank(fb, 0);
             ptx::tma_load_2d_pair(dst_a, &tmap_a, kb * BK, a_row, fb_leader);
             ptx::tma_load_2d_pair(dst_b, &tmap_b, kb * BK, b_row, fb_leader);
+            if constexpr (MX) {
+              ptx::tma_load_2d_pair(dst_sfa, &tmap_sfa, 0, sfa_row, fb_leader);
+              ptx::tma_load_2d_pair(dst_sfb, &tmap_sfb, 0, sfb_row, fb_leader);
+              ptx::tma_load_2d_pair(dst_sfb + 512, &tmap_sfb, 0, sfb_row + p.ncb, fb_leader);
+            }
           }
           ++issued;
           if (++stage == C::STAGES) {
@@ -257,8 +301,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!*abort) record_timeout(2u, abort);
           break;
         }
+        // MX: the previous tile's epilogue must also have read the chunk the accumulators
+        // share before this tile's first MMA overwrites it.
+        if (MX && it > 0 &&
+            !ptx::mbar_wait_bounded(bar_tovl, static_cast<uint32_t>(it - 1) & 1u, abort,
+                                    kWaitLimitNs)) {
+          if (!*abort) record_timeout(2u, abort);
+          break;
+        }
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + (acc ? C::ACC1_COL : 0u);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!ptx::mbar_wait_bounded(bar_full + 8 * stage, phase, abort, kWaitLimitNs)) {
             if (!*abort) record_timeout(2u, abort);
@@ -268,15 +320,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ptx::tc_fence_after();
           const uint64_t adesc = ptx::sw128_kmajor_desc(sbase + C::OFF_A + stage * A_STAGE);
           const uint64_t bdesc = ptx::sw128_kmajor_desc(sbase + C::OFF_B + stage * C::B_STAGE);
+          if constexpr (MX) {
+            // this K-block's scales into TMEM, ahead of its MMAs in the same pipe
+            const uint32_t sfa_s = sbase + C::OFF_SFA + stage * C::SFA_STAGE;
+            const uint32_t sfb_s = sbase + C::OFF_SFB + stage * C::SFB_STAGE;
+            ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFA_COL, ptx::sf_block_desc(sfa_s));
+            ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFB_COL, ptx::sf_block_desc(sfb_s));
+            ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFB_COL + 4,
+                                        ptx::sf_block_desc(sfb_s + 512));
+          }
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             // advance the start address by kk*32 bytes inside the swizzle atom
             const uint64_t koff = static_cast<uint64_t>((kk * UMMA_K) >> 4);
             const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
-            if constexpr (CG == 1)
+            if constexpr (MX) {
+              // scale byte kk of each 32-bit scale word: the kk-th 32-element block
+              const uint32_t sfid = static_cast<uint32_t>(kk) << 30;
+              ptx::mma_mxf8f6f4<CG>(d_tmem, adesc + koff, bdesc + koff,
+                                    C::IDESC_MX | ptx::idesc_mx_e4m3(0, 0, kk),
+                                    (tmem_base + C::SFA_COL) | sfid,
+                                    (tmem_base + C::SFB_COL) | sfid, accumulate);
+            } else if constexpr (CG == 1) {
               ptx::mma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, C::IDESC, accumulate);
-            else
+            } else {
               ptx::mma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, C::IDESC, accumulate);
+            }
           }
           // the stage is reusable (in both CTAs) once these MMAs have read it
           if constexpr (CG == 1)
@@ -324,7 +393,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int i = lane; i < BN; i += 32) {
         const int n = nt * BN + i;
         const bool in = n < p.N;
-        par_ws[i] = in ? __ldg(p.ws + n) : 0.0f;
+        par_ws[i] = in ? (MX ? 1.0f : __ldg(p.ws + n)) : 0.0f;  // MX: scales are in acc
         par_b[i] = in ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
       }
       __syncwarp();
@@ -335,14 +404,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::tc_fence_after();
       const int row0 = mt * C::TILE_M + static_cast<int>(rank) * BM + quarter * 32;
       const int row = row0 + lane;
-      const float xs = row < p.M ? __ldg(p.xs + row) : 0.0f;
+      const float xs = MX ? 1.0f : (row < p.M ? __ldg(p.xs + row) : 0.0f);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN);
+                             (acc ? C::ACC1_COL : 0u);
       const bool rows_live = row0 < p.M;  // a quarter wholly below M stores nothing
+      // MX: the chunk the two accumulators share (accumulator 0's last, accumulator 1's
+      // first) is read first and released on bar_tovl before the others.
+      bool ovl_done = !MX;
+      auto release_overlap = [&]() {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1)
+            ptx::mbar_arrive(bar_tovl);
+          else
+            ptx::mbar_arrive_cluster(ptx::map_shared_rank(bar_tovl, 0));
+        }
+        ovl_done = true;
+      };
 #pragma unroll 1
-      for (int c = 0; c < BN / EPI_COLS; ++c) {
+      for (int ci = 0; ci < BN / EPI_COLS; ++ci) {
+        if (MX && ci == 1 && !ovl_done) release_overlap();
+        const int c = (MX && acc == 0) ? (ci + BN / EPI_COLS - 1) % (BN / EPI_COLS) : ci;
         const int n0 = nt * BN + c * EPI_COLS;
-        if (n0 >= p.N || !rows_live) break;  // warp-uniform
+        if (!rows_live) break;   // warp-uniform
+        if (n0 >= p.N) {
+          if (MX) continue;      // chunk order is not ascending
+          break;
+        }
         uint32_t r[64];
         ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS),
                                 *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -433,6 +522,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         ++st_cnt;
       }
+      if (MX && !ovl_done) release_overlap();
       // All TMEM reads of this accumulator are complete (wait::ld above): release it to
       // the MMA issuer (the leader CTA's barrier for a pair).
       ptx::tc_fence_before();
@@ -508,7 +598,7 @@ struct LaunchInfo {
   int max_groups = 0;
 };
 
-template <int CG>
+template <int CG, bool MX>
 LaunchInfo &launch_info(int device, int sm_count) {
   static LaunchInfo info[64];
   static std::mutex mu;
@@ -516,14 +606,14 @@ LaunchInfo &launch_info(int device, int sm_count) {
   LaunchInfo &li = info[device & 63];
   if (!li.ready) {
     li.ready = true;
-    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(Cfg<CG>::SMEM_BYTES));
+    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(Cfg<CG, MX>::SMEM_BYTES));
     li.max_groups = sm_count / CG;
     if (li.err == cudaSuccess && CG == 2) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(sm_count);
       cfg.blockDim = dim3(NUM_THREADS);
-      cfg.dynamicSmemBytes = Cfg<CG>::SMEM_BYTES;
+      cfg.dynamicSmemBytes = Cfg<CG, MX>::SMEM_BYTES;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = CG;
@@ -532,7 +622,7 @@ LaunchInfo &launch_info(int device, int sm_count) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG>, &cfg);
+      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG, MX>, &cfg);
       if (li.err == cudaSuccess) li.max_groups = std::min(li.max_groups, clusters);
       if (li.err == cudaSuccess && li.max_groups < 1) li.err = cudaErrorInvalidConfiguration;
     }
@@ -540,11 +630,25 @@ LaunchInfo &launch_info(int device, int sm_count) {
   return li;
 }
 
-template <int CG>
+template <int CG, bool MX>
 int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
-  using C = Cfg<CG>;
+  using C = Cfg<CG, MX>;
   std::string err;
-  CUtensorMap ta, tb, tout;
+  CUtensorMap ta, tb, tout, tsfa, tsfb;
+  const int64_t ncb = (a.K + BK - 1) / BK;  // MX: scale tiles per 128-row block
+  if constexpr (MX) {
+    // the tiled e8m0 scale grids as [tiles, 128] arrays of 32-bit words: one row per
+    // 512-byte tile (128 rows x 4 scales), row = 128-row block * ncb + K-block
+    const uint64_t tiles_a = static_cast<uint64_t>((a.M + 127) / 128 * ncb);
+    const uint64_t tiles_b = static_cast<uint64_t>((a.N + 127) / 128 * ncb);
+    if (!make_tmap_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.xsf, 128, tiles_a, 512, 128, 1,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, &err) ||
+        !make_tmap_2d(&tsfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.wsf, 128, tiles_b, 512, 128, 1,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, &err)) {
+      set_error("mxfp8_gemm: " + err);
+      return 4;
+    }
+  }
   const int64_t ldo = a.ldo > 0 ? a.ldo : a.N;
   const bool direct = (a.N % 8) != 0 || (ldo % 8) != 0 ||
                       (reinterpret_cast<uintptr_t>(a.out) % 16) != 0;
@@ -576,6 +680,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   p.m_tiles = static_cast<int>((a.M + C::TILE_M - 1) / C::TILE_M);
   p.n_tiles = static_cast<int>((a.N + BN - 1) / BN);
   p.k_blocks = static_cast<int>((a.K + BK - 1) / BK);
+  p.ncb = static_cast<int>(ncb);
   p.n_fastest = a.M >= a.N ? 1 : 0;
   p.direct_store = direct ? 1 : 0;
   p.out = a.out;
@@ -593,7 +698,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
     set_error("fp8_gemm: too many output tiles");
     return 2;
   }
-  LaunchInfo &li = launch_info<CG>(dev.device, dev.sm_count);
+  LaunchInfo &li = launch_info<CG, MX>(dev.device, dev.sm_count);
   if (li.err != cudaSuccess) {
     set_error(std::string("fp8_gemm: kernel setup: ") + cudaGetErrorString(li.err));
     return 4;
@@ -621,7 +726,11 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG>, ta, tb, tout, p);
+  if constexpr (!MX) {  // unused by the kernel: any valid map
+    tsfa = ta;
+    tsfb = ta;
+  }
+  cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, MX>, ta, tb, tout, tsfa, tsfb, p);
   if (ce != cudaSuccess) {
     set_error(std::string("fp8_gemm: launch failed: ") + cudaGetErrorString(ce));
     return 4;
@@ -651,11 +760,20 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     set_error("fp8_gemm: dimensions must fit in int32 and at most 7 peers");
     return 2;
   }
+  // MXFP8: single CTAs with 128-row tiles for M <= 128, CTA pairs otherwise.
+  if (a.mx) {
+    if (a.n_peers != 0) {
+      set_error("mxfp8_gemm: peer outputs are not supported");
+      return 2;
+    }
+    if (a.M <= gemm::BM) return gemm::launch_shape<1, true>(a, dev, stream, pdl);
+    return gemm::launch_shape<2, true>(a, dev, stream, pdl);
+  }
   // Few tokens: stream the weights with swap-AB split-K tiles. Otherwise CTA pairs with
   // 256-row tiles (or single CTAs with 128-row tiles for peer outputs at M <= 128).
   if (a.M <= gemm::BM && a.n_peers == 0) return launch_gemm_small(a, stream, pdl);
-  if (a.M <= gemm::BM) return gemm::launch_shape<1>(a, dev, stream, pdl);
-  return gemm::launch_shape<2>(a, dev, stream, pdl);
+  if (a.M <= gemm::BM) return gemm::launch_shape<1, false>(a, dev, stream, pdl);
+  return gemm::launch_shape<2, false>(a, dev, stream, pdl);
 }
 
 namespace {

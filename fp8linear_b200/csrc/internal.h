@@ -65,6 +65,11 @@ struct GemmArgs {
   // same layout as `out`), straight from the epilogue.
   int n_peers = 0;
   void *const *peers = nullptr;
+  // MXFP8 (block-scaled) form: xs/ws unused; xsf/wsf are the tiled e8m0 scale grids of
+  // xq and wq (mx_scale_bytes(M, K) / mx_scale_bytes(N, K), 16-byte aligned).
+  bool mx = false;
+  const uint8_t *xsf = nullptr;
+  const uint8_t *wsf = nullptr;
 };
 constexpr int kMaxPeers = 7;
 // Launches the tcgen05 GEMM + fused epilogue. `pdl` launches it as a programmatic

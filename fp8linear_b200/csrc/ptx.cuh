@@ -284,6 +284,44 @@ __device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc
       : "memory");
 }
 
+// Block-scaled (MXFP8) form: D (+)= (A * 2^(sfA)) * (B * 2^(sfB))^T with one e8m0 scale per
+// 32 K-elements of every row of A and B, read from TMEM at `sfa` / `sfb` (the byte of the
+// 32-bit scale word selected by bits 30-31 of the address and the instruction
+// descriptor's scale-factor ids). CG = 2: issued by the pair's leader.
+template <int CG>
+__device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                             uint32_t accumulate) {
+  if constexpr (CG == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+// Copy a 32-row x 128-bit block of scale factors from shared memory (descriptor) into
+// TMEM at `taddr`, broadcast to all four 32-lane quarters (.32x128b.warpx4): lane
+// 32w + i receives row i. CG = 2: issued by the leader, each CTA copying its own
+// shared memory into its own TMEM.
+template <int CG>
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  if constexpr (CG == 1)
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+                 : "memory");
+  else
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+                 : "memory");
+}
+
 // Arrive (once) on `bar` when all tcgen05 ops issued so far by this thread complete.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile(
@@ -369,6 +407,26 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;
   return d;
+}
+
+// Shared-memory descriptor of a 32-row x 16-byte block stored contiguously (rows 16 B
+// apart), no swizzle: 8-row core matrices of 128 B, SBO = 128 B between them (LBO unused,
+// one core matrix along K), descriptor version 1, layout SWIZZLE_NONE (0).
+__device__ __forceinline__ uint64_t sf_block_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(128u >> 4) << 16;
+  d |= static_cast<uint64_t>(128u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  return d;
+}
+
+// Instruction descriptor for kind::mxf8f6f4.block_scale: A/B e4m3 (format 0, bits 7-9 and
+// 10-12), both K-major, N>>3 in bits 17-22, scale type e8m0 (bit 23 = 1), M>>4 in bits
+// 24-28, the scale-factor byte ids of B (bits 4-5) and A (bits 29-30). D is fp32.
+__host__ __device__ constexpr uint32_t idesc_mx_e4m3(int m, int n, uint32_t sf_id) {
+  return ((sf_id & 3u) << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) |
+         (static_cast<uint32_t>(m >> 4) << 24) | ((sf_id & 3u) << 29);
 }
 
 // Instruction descriptor for kind::f8f6f4: D f32 (bits 4-5 = 1), A/B e4m3 (format 0),

@@ -11,8 +11,9 @@ Same public names and contracts:
 
 Differences from the reference: ``fp8_linear`` returns ``x.dtype`` (the reference
 returns fp16 and ``Fp8Linear.forward`` casts back); ``fp8_gemm`` returns bf16; the
-MXFP8 quantizer (``quantize_mxfp8`` / ``quantize_weight_mxfp8``) is implemented; the
-remaining MXFP8 / NVFP4 entry points exist but raise ``NotImplementedError``.
+MXFP8 path (``quantize_mxfp8``, ``quantize_weight_mxfp8``, ``mxfp8_gemm``,
+``mxfp8_linear``, and ``fp8_linear`` on uint8 block scales) is implemented; the NVFP4
+entry points exist but raise ``NotImplementedError``.
 """
 from __future__ import annotations
 
@@ -57,6 +58,16 @@ def mx_scale_bytes(rows: int, K: int) -> int:
     return ((rows + 127) // 128) * ((K // MX_BLOCK + 3) // 4) * 512
 
 
+@torch.library.register_fake(add_op_namespace_prefix("mxfp8_gemm"))
+def _mxfp8_gemm_fake(xq, x_scales, wq, w_scales, bias=None):
+    return xq.new_empty((xq.shape[0], wq.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.register_fake(add_op_namespace_prefix("mxfp8_linear"))
+def _mxfp8_linear_fake(x, wq, w_scales, bias=None):
+    return x.new_empty((*x.shape[:-1], wq.shape[0]), dtype=x.dtype)
+
+
 @torch.library.register_fake(add_op_namespace_prefix("quantize_mxfp8"))
 def _quantize_mxfp8_fake(x):
     xq = x.new_empty(x.shape, dtype=torch.float8_e4m3fn)
@@ -66,8 +77,8 @@ def _quantize_mxfp8_fake(x):
 
 def _not_provided(name: str):
     raise NotImplementedError(
-        f"{name}: fp8linear_b200 implements the per-channel FP8 path only "
-        "(quantize_fp8 / quantize_weight / fp8_gemm / fp8_linear)"
+        f"{name}: fp8linear_b200 implements the per-channel FP8 and the MXFP8 paths; "
+        "NVFP4 is not provided"
     )
 
 
@@ -83,8 +94,11 @@ def quantize_weight_mxfp8(weight: torch.Tensor):
 
 
 def mxfp8_linear(x, wq, w_scales, bias=None):
-    """Not provided (the reference's opt-in MXFP8 format); raises NotImplementedError."""
-    _not_provided("mxfp8_linear")
+    """MXFP8 linear (layers.py:84-86 of the reference): ``wq``/``w_scales`` from
+    ``quantize_weight_mxfp8``; ``x [..., K]`` is block-quantized on the fly and multiplied
+    by the block-scaled tcgen05 GEMM (scales applied inside the MMA, bias fused);
+    returns ``x.dtype``."""
+    return ops.mxfp8_linear(x, wq, w_scales, bias)
 
 
 def quantize_weight_nvfp4(weight: torch.Tensor):

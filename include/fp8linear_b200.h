@@ -127,6 +127,37 @@ FP8LIN_API int fp8lin_fp8_gemm(const void *xq, const float *x_scale, const void 
                                void *stream);
 
 /*
+ * MXFP8 GEMM with block scales applied inside the tensor-core MMA and the bias fused.
+ * Replaces mxfp8_gemm (csrc/fp8_gemm.cu:233-340: cuBLASLt VEC32_UE8M0 block-scaled matmul,
+ * bias epilogue, fp16 out), here one tcgen05 kind::mxf8f6f4.block_scale kernel:
+ *   out[m,n] = sum_k xq[m,k] 2^(xs[m,k/32]-127) * wq[n,k] 2^(ws[n,k/32]-127) + bias[n]
+ *   xq [M,K], wq [N,K] e4m3 row-major, 16-byte aligned; K % 32 == 0
+ *   x_scales / w_scales: the tiled e8m0 grids of fp8lin_quantize_mxfp8 for M / N rows
+ *   (fp8lin_mx_scale_bytes bytes), 16-byte aligned
+ *   bias [N] BF16/F16/F32 or NULL; out [M,N] BF16 or F16 (the reference writes fp16)
+ * M == 0 or N == 0 is a no-op.
+ */
+FP8LIN_API int fp8lin_mxfp8_gemm(const void *xq, const void *x_scales, const void *wq,
+                                 const void *w_scales, const void *bias, int bias_dtype,
+                                 void *out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                 void *stream);
+
+/* Workspace fp8lin_mxfp8_linear needs: the codes (M*K) and the scale grid, each rounded
+ * up to 256 bytes. */
+FP8LIN_API size_t fp8lin_mxfp8_linear_workspace_size(int64_t M, int64_t K);
+
+/*
+ * Fused MXFP8 linear: fp8lin_quantize_mxfp8 of x into the workspace, then the block-scaled
+ * GEMM launched as its programmatic dependent. Replaces mxfp8_linear
+ * (csrc/fp8_gemm.cu:335-345) and the MXFP8 branch of fp8_linear (csrc/fp8_gemm.cu:206-213).
+ * wq / w_scales from fp8lin_quantize_mxfp8 of the weight (quantize_weight_mxfp8).
+ */
+FP8LIN_API int fp8lin_mxfp8_linear(const void *x, int x_dtype, const void *wq,
+                                   const void *w_scales, const void *bias, int bias_dtype,
+                                   void *out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                   void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Device workspace fp8lin_fp8_linear needs for M tokens of width K: the e4m3 codes
  * and the per-token scales of x (aligned sub-buffers).
  */

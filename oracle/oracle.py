@@ -19,7 +19,7 @@ Reference citations (paths relative to the reference project root):
   GEMM + dequant/bias  csrc/fp8_gemm.cu:139-194, dequant_bias_kernel :65-80
   fused entry          csrc/fp8_gemm.cu:196-221
   MXFP8 block quant    csrc/quantize.cu:75-131 (layout + kernel), :239-285 (host op)
-  MXFP8 GEMM           csrc/fp8_gemm.cu:233-340 (cuBLASLt VEC32_UE8M0, bias, fp16 out)
+  MXFP8 GEMM           csrc/fp8_gemm.cu:233-333 (cuBLASLt VEC32_UE8M0, bias, fp16 out)
 """
 from __future__ import annotations
 

@@ -101,12 +101,14 @@ def test_quantize_and_fp8linear_module():
     assert rel < 0.1
 
 
-def test_linear_rejects_block_scaled_formats():
+def test_linear_rejects_nvfp4_weights():
+    """uint8 scales with an e4m3 weight are MXFP8 (tests/test_mx_gemm_gpu.py); with a packed
+    uint8 weight they are NVFP4, which is not provided and raises."""
     import fp8linear_b200 as f
 
     x = torch.randn(4, 64, device="cuda", dtype=torch.bfloat16)
-    wq = torch.zeros(16, 64, dtype=torch.float8_e4m3fn, device="cuda")
-    with pytest.raises(RuntimeError, match="not supported"):
-        f.fp8_linear(x, wq, torch.zeros(512, dtype=torch.uint8, device="cuda"), None)
+    wq4 = torch.zeros(16, 32, dtype=torch.uint8, device="cuda")
+    with pytest.raises(RuntimeError, match="NVFP4"):
+        f.fp8_linear(x, wq4, torch.zeros(512, dtype=torch.uint8, device="cuda"), None)
     with pytest.raises(NotImplementedError):
         f.quantize_weight_nvfp4(x)

@@ -66,7 +66,9 @@ def test_block_scaled_entry_points_raise():
     # the MXFP8 quantizer exists but, like every op here, has no CPU kernel
     with pytest.raises((RuntimeError, NotImplementedError)):
         f.quantize_weight_mxfp8(torch.zeros(4, 32))
-    with pytest.raises(NotImplementedError):
-        f.mxfp8_linear(None, None, None)
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        f.mxfp8_linear(torch.zeros(2, 32, dtype=torch.bfloat16),
+                       torch.zeros(4, 32, dtype=torch.float8_e4m3fn),
+                       torch.zeros(512, dtype=torch.uint8))
     with pytest.raises(NotImplementedError):
         f.nvfp4_linear(None, None, None)
