@@ -23,7 +23,7 @@
  *   oracle_quantize_mxfp8   quant_mxfp8_kernel (csrc/quantize.cu:92-131), launched by
  *                           quantize_mxfp8 (csrc/quantize.cu:239-285)
  *   oracle_mxfp8_gemm       cuBLASLt VEC32_UE8M0 block-scaled e4m3 matmul with the bias
- *                           epilogue, fp16 out (csrc/fp8_gemm.cu:233-340)
+ *                           epilogue, fp16 out (csrc/fp8_gemm.cu:233-333)
  *
  * Arithmetic is IEEE binary32 with round-to-nearest-even and no flush-to-zero,
  * which is what nvcc emits for the reference without --use_fast_math.
@@ -295,7 +295,7 @@ void oracle_quantize_mxfp8(const uint16_t *x, int dtype, int64_t M, int64_t K, u
 }
 
 /*
- * MXFP8 GEMM, csrc/fp8_gemm.cu:233-340: D = A * B with per-32 e8m0 block scales on both
+ * MXFP8 GEMM, csrc/fp8_gemm.cu:233-333: D = A * B with per-32 e8m0 block scales on both
  * operands, bias epilogue, fp16 out:
  *   acc[m,n] = sum_k e4m3(xq[m,k]) 2^(xs[m,k/32]-127) * e4m3(wq[n,k]) 2^(ws[n,k/32]-127)
  *              (each term exact in double; the sum in double, rounded once to fp32)
