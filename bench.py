@@ -192,10 +192,11 @@ def set_count(per_set_bytes: int, dev, lo: int = 3, hi: int = 512) -> int:
     return max(lo, min(hi, need))
 
 
-def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True):
+def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True, fmt: str = "fp8"):
     """``n_sets`` independent (x, wq, ws, bias[, xq, xs]) sets of workload ``wl`` on
     the current device (weights quantized once, as offline). Set i's weight depends
-    only on i, so ranks hold the same weights; activations use ``x_seed0``."""
+    only on i, so ranks hold the same weights; activations use ``x_seed0``. ``fmt``
+    "fp8": per-token / per-channel scales; "mx": MXFP8 block scales."""
     import fp8linear_b200 as f
     from fp8linear_b200.workloads import make_weight, make_x
 
@@ -203,11 +204,11 @@ def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True):
     for i in range(n_sets):
         x = make_x(wl, seed=x_seed0 + 7919 * i, gen_device="cuda")
         w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
-        wq, ws = f.quantize_weight(w)
+        wq, ws = f.quantize_weight_mxfp8(w) if fmt == "mx" else f.quantize_weight(w)
         del w
         s = {"x": x, "wq": wq, "ws": ws, "b": b}
         if quantize_x:
-            s["xq"], s["xs"] = f.quantize_fp8(x)
+            s["xq"], s["xs"] = f.quantize_mxfp8(x) if fmt == "mx" else f.quantize_fp8(x)
         sets.append(s)
     return sets
 
@@ -461,19 +462,21 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
-def measure_workload(name: str, steps: int, warmup: int) -> dict:
+def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> dict:
     """Per-workload device times of the fused op, the GEMM alone and the quantizer
     alone: each is ``max(steps, sets)`` launches back to back in one CUDA graph over
-    rotating operand sets (inputs larger than L2), averaged per launch."""
+    rotating operand sets (inputs larger than L2), averaged per launch. ``fmt`` "mx":
+    the MXFP8 ops (mxfp8_linear, mxfp8_gemm, quantize_mxfp8) instead."""
     import fp8linear_b200 as f
     from fp8linear_b200.workloads import WORKLOADS
 
     wl = WORKLOADS[name]
     dev = torch.device("cuda", torch.cuda.current_device())
     n_sets = set_count(per_set_bytes(wl), dev)
-    sets = operand_sets(wl, n_sets)
+    sets = operand_sets(wl, n_sets, fmt=fmt)
     stream = torch.cuda.current_stream(dev)
     reps = max(steps, n_sets)
+    mx = fmt == "mx"
 
     def timed(call):
         for i in range(warmup):
@@ -483,25 +486,29 @@ def measure_workload(name: str, steps: int, warmup: int) -> dict:
         del g
         return ms
 
-    fused = timed(lambda st: f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"]))
-    gemm = timed(lambda st: f.fp8_gemm(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
-    quant = timed(lambda st: f.quantize_fp8(st["x"]))
+    lin_op, gemm_op, quant_op = ((f.mxfp8_linear, f.mxfp8_gemm, f.quantize_mxfp8) if mx else
+                                 (f.fp8_linear, f.fp8_gemm, f.quantize_fp8))
+    fused = timed(lambda st: lin_op(st["x"], st["wq"], st["ws"], st["b"]))
+    gemm = timed(lambda st: gemm_op(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
+    quant = timed(lambda st: quant_op(st["x"]))
+    # quantizer bytes: read 2MK, write MK codes + scales (4M fp32, or M*K/32 e8m0)
+    qbytes = wl.M * 3 * wl.K + (wl.M * wl.K // 32 if mx else 4 * wl.M)
     pk = peaks()
     # bandwidth-aware roofline for the GEMM: min(tensor peak, AI x HBM)
     ai = wl.flops / wl.gemm_bytes
     roof = min(2.0 * pk["bf16_tflops"], ai * pk["hbm_gbs"] / 1e3)
     g_tf = wl.flops / (gemm * 1e-3) / 1e12
-    return {"workload": name, "M": wl.M, "K": wl.K, "N": wl.N, "sets": n_sets,
+    return {"workload": name, "format": fmt, "M": wl.M, "K": wl.K, "N": wl.N, "sets": n_sets,
             "fused_us": round(fused * 1e3, 2),
             "fused_tflops": round(wl.flops / (fused * 1e-3) / 1e12, 1),
             "gemm_us": round(gemm * 1e3, 2), "gemm_tflops": round(g_tf, 1),
             "gemm_roofline_tflops": round(roof, 1), "gemm_frac": round(g_tf / roof, 4),
             "quant_us": round(quant * 1e3, 2),
-            "quant_gbs": round(wl.quant_bytes / (quant * 1e-3) / 1e9, 1),
-            "quant_frac": round(wl.quant_bytes / (quant * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+            "quant_gbs": round(qbytes / (quant * 1e-3) / 1e9, 1),
+            "quant_frac": round(qbytes / (quant * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
 
 
-def reference_workload(name: str, steps: int, warmup: int) -> dict:
+def reference_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> dict:
     """Device time of the reference's own compiled ops on one workload."""
     from fp8linear_b200.workloads import WORKLOADS
 
@@ -512,10 +519,12 @@ def reference_workload(name: str, steps: int, warmup: int) -> dict:
 
     a = A()
     a.steps, a.warmup = steps, warmup
-    r = reference_gpu_timing(wl, a)
+    r = reference_gpu_timing(wl, a, fmt)
     if r and "ms_per_step" in r:
-        r = {"workload": name, "ref_fused_us": round(r["ms_per_step"] * 1e3, 2),
+        r = {"workload": name, "format": fmt, "ref_fused_us": round(r["ms_per_step"] * 1e3, 2),
              "ref_fused_tflops": r["value"]}
+    else:
+        r = {"workload": name, "format": fmt, **(r or {})}
     return r
 
 
@@ -525,8 +534,8 @@ def run_sweep(args):
     torch.cuda.set_device(0)
     names = args.sweep.split(",") if args.sweep != "all" else list(WORKLOADS)
     for n in names:
-        r = reference_workload(n, args.steps, args.warmup) if args.impl == "reference" \
-            else measure_workload(n, args.steps, args.warmup)
+        r = reference_workload(n, args.steps, args.warmup, args.format) \
+            if args.impl == "reference" else measure_workload(n, args.steps, args.warmup, args.format)
         print(json.dumps(r), flush=True)
         torch.cuda.empty_cache()
 
@@ -677,10 +686,11 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def reference_gpu_timing(wl, args):
+def reference_gpu_timing(wl, args, fmt: str = "fp8"):
     """Device time of the reference's own compiled CUDA ops (cuBLASLt FP8 GEMM + dequant
     kernel, fp16 out, then the .to(bf16) cast Fp8Linear.forward applies), if built,
-    timed like our op: launches back to back over rotating operand sets."""
+    timed like our op: launches back to back over rotating operand sets. ``fmt`` "mx":
+    its mxfp8_linear (quantize_mxfp8 + cuBLASLt VEC32_UE8M0 GEMM with bias, fp16 out)."""
     try:
         from oracle import build_ref
         ref = build_ref.load()
@@ -697,14 +707,19 @@ def reference_gpu_timing(wl, args):
     for i in range(n_sets):
         x = make_x(wl, seed=7919 * i, gen_device="cuda")
         w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
-        wq, ws = ref.quantize_weight(w)
+        wq, ws = ref.quantize_mxfp8(w) if fmt == "mx" else ref.quantize_weight(w)
         sets.append({"x": x, "wq": wq, "ws": ws, "b": b})
         del w
     stream = torch.cuda.current_stream(dev)
+    lin = ref.mxfp8_linear if fmt == "mx" else ref.fp8_linear
 
     def call(st):
-        return ref.fp8_linear(st["x"], st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
+        return lin(st["x"], st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
 
+    try:
+        call(sets[0])
+    except RuntimeError as e:  # e.g. cuBLASLt offers no MXFP8 algorithm for a few tokens
+        return {"unavailable": f"the reference op raised: {str(e).splitlines()[0][:160]}"}
     for i in range(max(3, args.warmup)):
         call(sets[i % n_sets])
     reps = max(args.steps, n_sets)
@@ -746,6 +761,8 @@ def main():
                          "channels with an NCCL all-gather")
     ap.add_argument("--fused", action="store_true",
                     help="with --mode nshard: fuse the all-gather into the GEMM epilogue")
+    ap.add_argument("--format", choices=["fp8", "mx"], default="fp8",
+                    help="with --sweep: per-channel FP8 ops (default) or the MXFP8 ops")
     ap.add_argument("--sweep", default="",
                     help="'all' or comma-separated workloads: one JSON line of per-kernel "
                          "device times per workload (not the driver's line)")
