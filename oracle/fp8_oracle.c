@@ -22,6 +22,10 @@
  *   oracle_mx_sf_offset     the tiled block-scale layout sf_offset (csrc/quantize.cu:75-83)
  *   oracle_quantize_mxfp8   quant_mxfp8_kernel (csrc/quantize.cu:92-131), launched by
  *                           quantize_mxfp8 (csrc/quantize.cu:239-285)
+ *   oracle_quantize_nvfp4   quant_nvfp4_kernel + f2e2m1 (csrc/quantize.cu:136-194),
+ *                           launched by quantize_nvfp4 (csrc/quantize.cu:290-334)
+ *   oracle_nvfp4_gemm       the block-scaled e2m1 product nvfp4_gemm asks cuBLASLt for
+ *                           (VEC16_UE4M3, bias epilogue, fp16 out; csrc/fp8_gemm.cu:347-446)
  *   oracle_mxfp8_gemm       cuBLASLt VEC32_UE8M0 block-scaled e4m3 matmul with the bias
  *                           epilogue, fp16 out (csrc/fp8_gemm.cu:233-333)
  *
@@ -318,6 +322,111 @@ void oracle_mxfp8_gemm(const uint8_t *xq, const uint8_t *xs, const uint8_t *wq,
         double part = 0.0;
         for (int64_t j = 0; j < 32; ++j)
           part += (double)lut[xq[m * K + g * 32 + j]] * (double)lut[wq[n * K + g * 32 + j]];
+        s += part * sa * sb;
+      }
+      volatile float v = (float)s;
+      if (bias16) v = v + oracle_f16_to_f32(bias16[n]);
+      out[m * N + n] = round_out ? oracle_f16_to_f32(oracle_f32_to_f16(v)) : v;
+    }
+  }
+}
+
+/*
+ * NVFP4 e2m1 encoding of csrc/quantize.cu:136-150: sign bit 8 when v < 0 (so -0.0 and
+ * NaN get no sign), magnitude code by thresholds (ties go up):
+ * |v| < 0.25 -> 0, < 0.75 -> 1 (0.5), < 1.25 -> 2 (1), < 1.75 -> 3 (1.5), < 2.5 -> 4 (2),
+ * < 3.5 -> 5 (3), < 5 -> 6 (4), else 7 (6).
+ */
+uint8_t oracle_e2m1_encode(float v) {
+  uint8_t s = v < 0.0f ? 8 : 0;
+  float a = fabsf(v);
+  uint8_t c;
+  if (a < 0.25f) c = 0;
+  else if (a < 0.75f) c = 1;
+  else if (a < 1.25f) c = 2;
+  else if (a < 1.75f) c = 3;
+  else if (a < 2.5f) c = 4;
+  else if (a < 3.5f) c = 5;
+  else if (a < 5.0f) c = 6;
+  else c = 7;
+  return (uint8_t)(s | c);
+}
+
+float oracle_e2m1_decode(uint8_t c) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  float v = mag[c & 7];
+  return (c & 8) ? -v : v;
+}
+
+/* Bytes of the NVFP4 scale grid: 16-element blocks, so ceil((K / 16) / 4) tile columns. */
+int64_t oracle_nv_sf_bytes(int64_t rows, int64_t K) {
+  return ((rows + 127) / 128) * ((K / 16 + 3) / 4) * 512;
+}
+
+/*
+ * NVFP4 quantization, csrc/quantize.cu:157-194 (one 16-element block of a row):
+ *   amax  = fmaxf-reduce |x| (NaN ignored unless the block is all NaN)
+ *   s     = fminf(amax * fl(1/6), 448)      (fminf ignores a NaN amax: 448)
+ *   s8    = e4m3_satfinite(s), sdec = decode(s8)
+ *   x_inv = sdec > 0 ? 1 / sdec : 0         (IEEE divide)
+ *   code  = e2m1(fminf(fmaxf(x * x_inv, -6), 6))
+ * Codes pack two per byte, element 2j in the low nibble; scales land at
+ * oracle_mx_sf_offset(row, block, ncb) of a grid prefilled with 0x38 (e4m3 1.0).
+ */
+void oracle_quantize_nvfp4(const uint16_t *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                           uint8_t *scales) {
+  const int64_t nblk = K / 16, ncb = (nblk + 3) / 4;
+  const float inv6 = 1.0f / 6.0f;
+  memset(scales, 0x38, (size_t)oracle_nv_sf_bytes(M, K));
+  for (int64_t r = 0; r < M; ++r) {
+    for (int64_t g = 0; g < nblk; ++g) {
+      const uint16_t *blk = x + r * K + g * 16;
+      float v[16];
+      float amax = 0.0f;
+      for (int j = 0; j < 16; ++j) {
+        v[j] = dtype ? oracle_f16_to_f32(blk[j]) : oracle_bf16_to_f32(blk[j]);
+        float a = fabsf(v[j]);
+        amax = j == 0 ? a : fmaxf(amax, a);
+      }
+      volatile float sp = amax * inv6;
+      float sc = fminf(sp, E4M3_MAX);
+      uint8_t s8 = oracle_e4m3_encode(sc, 1);
+      float sdec = oracle_e4m3_decode(s8);
+      volatile float x_inv = sdec > 0.0f ? 1.0f / sdec : 0.0f;
+      scales[oracle_mx_sf_offset(r, g, ncb)] = s8;
+      for (int j = 0; j < 16; j += 2) {
+        volatile float p0 = v[j] * x_inv, p1 = v[j + 1] * x_inv;
+        uint8_t lo = oracle_e2m1_encode(fminf(fmaxf(p0, -6.0f), 6.0f));
+        uint8_t hi = oracle_e2m1_encode(fminf(fmaxf(p1, -6.0f), 6.0f));
+        xq[(r * K + g * 16 + j) / 2] = (uint8_t)(lo | (hi << 4));
+      }
+    }
+  }
+}
+
+/*
+ * NVFP4 GEMM: out[m,n] = sum_k e2m1(xq[m,k]) s_x[m,k/16] * e2m1(wq[n,k]) s_w[n,k/16]
+ * + float(bias16[n]); the scales are e4m3 bytes of the tiled grids; each term exact
+ * in double, the sum in double rounded once to fp32; round_out rounds to fp16.
+ * xq / wq: packed [rows, K/2].
+ */
+void oracle_nvfp4_gemm(const uint8_t *xq, const uint8_t *xs, const uint8_t *wq,
+                       const uint8_t *ws, const uint16_t *bias16, int64_t M, int64_t N,
+                       int64_t K, int round_out, float *out) {
+  const int64_t nblk = K / 16, ncb = (nblk + 3) / 4;
+  for (int64_t m = 0; m < M; ++m) {
+    for (int64_t n = 0; n < N; ++n) {
+      double s = 0.0;
+      for (int64_t g = 0; g < nblk; ++g) {
+        const double sa = oracle_e4m3_decode(xs[oracle_mx_sf_offset(m, g, ncb)]);
+        const double sb = oracle_e4m3_decode(ws[oracle_mx_sf_offset(n, g, ncb)]);
+        double part = 0.0;
+        for (int64_t j = 0; j < 16; ++j) {
+          const int64_t k = g * 16 + j;
+          const uint8_t a = (uint8_t)((xq[(m * K + k) / 2] >> ((k & 1) * 4)) & 15);
+          const uint8_t b = (uint8_t)((wq[(n * K + k) / 2] >> ((k & 1) * 4)) & 15);
+          part += (double)oracle_e2m1_decode(a) * (double)oracle_e2m1_decode(b);
+        }
         s += part * sa * sb;
       }
       volatile float v = (float)s;

@@ -20,6 +20,8 @@ Reference citations (paths relative to the reference project root):
   fused entry          csrc/fp8_gemm.cu:196-221
   MXFP8 block quant    csrc/quantize.cu:75-131 (layout + kernel), :239-285 (host op)
   MXFP8 GEMM           csrc/fp8_gemm.cu:233-333 (cuBLASLt VEC32_UE8M0, bias, fp16 out)
+  NVFP4 quant          csrc/quantize.cu:136-194 (f2e2m1 + kernel), :290-334 (host op)
+  NVFP4 GEMM           csrc/fp8_gemm.cu:347-446 (cuBLASLt VEC16_UE4M3, bias, fp16 out)
 """
 from __future__ import annotations
 
@@ -84,6 +86,10 @@ def lib() -> ctypes.CDLL:
         L.oracle_quantize_mxfp8.restype = None
         L.oracle_mxfp8_gemm.argtypes = [P, P, P, P, P, i64, i64, i64, ctypes.c_int, P]
         L.oracle_mxfp8_gemm.restype = None
+        L.oracle_quantize_nvfp4.argtypes = [P, ctypes.c_int, i64, i64, P, P]
+        L.oracle_quantize_nvfp4.restype = None
+        L.oracle_nvfp4_gemm.argtypes = [P, P, P, P, P, i64, i64, i64, ctypes.c_int, P]
+        L.oracle_nvfp4_gemm.restype = None
         _lib = L
     return _lib
 
@@ -163,6 +169,36 @@ def c_mxfp8_gemm(xq, xs, wq, ws, bias16=None, round_out=True):
     N = wq.shape[0]
     out = np.empty((M, N), np.float32)
     lib().oracle_mxfp8_gemm(_ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws), _ptr(bias16), M, N, K,
+                            int(round_out), _ptr(out))
+    return out
+
+
+def nv_sf_bytes(rows: int, K: int) -> int:
+    """Bytes of the NVFP4 scale grid: ceil(rows/128) * ceil((K/16)/4) * 512."""
+    return ((rows + 127) // 128) * ((K // 16 + 3) // 4) * 512
+
+
+def c_quantize_nvfp4(x16: np.ndarray, dtype: int = BF16):
+    """NVFP4 packed codes [M, K/2] and the tiled e4m3 scale grid (1-D uint8)."""
+    x16 = np.ascontiguousarray(x16, dtype=np.uint16)
+    M, K = x16.shape
+    xq = np.empty((M, K // 2), np.uint8)
+    sc = np.empty((nv_sf_bytes(M, K),), np.uint8)
+    lib().oracle_quantize_nvfp4(_ptr(x16), dtype, M, K, _ptr(xq), _ptr(sc))
+    return xq, sc
+
+
+def c_nvfp4_gemm(xq, xs, wq, ws, bias16=None, round_out=True):
+    xq = np.ascontiguousarray(xq, np.uint8)
+    wq = np.ascontiguousarray(wq, np.uint8)
+    xs = np.ascontiguousarray(xs, np.uint8)
+    ws = np.ascontiguousarray(ws, np.uint8)
+    if bias16 is not None:
+        bias16 = np.ascontiguousarray(bias16, np.uint16)
+    M, K = xq.shape[0], xq.shape[1] * 2
+    N = wq.shape[0]
+    out = np.empty((M, N), np.float32)
+    lib().oracle_nvfp4_gemm(_ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws), _ptr(bias16), M, N, K,
                             int(round_out), _ptr(out))
     return out
 
@@ -386,6 +422,75 @@ def np_mx_decode(q: np.ndarray, sc: np.ndarray) -> np.ndarray:
 def np_mxfp8_gemm(xq, xs, wq, ws, bias16=None, round_out=False):
     """Decoded float64 matmul (twin of c_mxfp8_gemm up to summation order)."""
     acc = (np_mx_decode(xq, xs) @ np_mx_decode(wq, ws).T).astype(np.float32)
+    if bias16 is not None:
+        acc = acc + f16_bits_to_f32(np.asarray(bias16, np.uint16))[None, :]
+    if round_out:
+        acc = acc.astype(np.float16).astype(np.float32)
+    return acc
+
+
+# ----------------------------------------------------------------------------- NVFP4 numpy twins
+
+E2M1_MAG = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], np.float32)
+
+
+def np_e2m1_encode(v: np.ndarray) -> np.ndarray:
+    """Vectorised oracle_e2m1_encode (threshold rounding, sign only for v < 0)."""
+    v = np.asarray(v, np.float32)
+    with np.errstate(invalid="ignore"):
+        s = np.where(v < 0, 8, 0).astype(np.uint8)
+    a = np.abs(v)
+    c = np.searchsorted(np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32), a,
+                        side="right").astype(np.uint8)
+    c = np.where(np.isnan(a), 7, c)  # unreachable after the clamp; NaN sorts last
+    return s | c
+
+
+def np_quantize_nvfp4(x16: np.ndarray, dtype: int = BF16):
+    """Vectorised twin of c_quantize_nvfp4."""
+    x16 = np.ascontiguousarray(x16, dtype=np.uint16)
+    M, K = x16.shape
+    nblk, ncb = K // 16, (K // 16 + 3) // 4
+    x = bf16_bits_to_f32(x16) if dtype == BF16 else f16_bits_to_f32(x16)
+    blk = x.reshape(M, nblk, 16)
+    a = np.abs(blk)
+    all_nan = np.all(np.isnan(a), axis=2)
+    amax = np.max(np.where(np.isnan(a), np.float32(-1.0), a), axis=2).astype(np.float32)
+    amax = np.where(all_nan, np.float32(np.nan), amax).astype(np.float32)
+    inv6 = np.float32(1.0) / np.float32(6.0)
+    with np.errstate(invalid="ignore", over="ignore"):
+        sp = (amax * inv6).astype(np.float32)
+    sc = np.where(np.isnan(sp), E4M3_MAX, np.minimum(sp, E4M3_MAX)).astype(np.float32)
+    s8 = np_e4m3_encode(sc, saturate=True)
+    sdec = e4m3_decode_lut()[s8].astype(np.float32)
+    with np.errstate(divide="ignore"):
+        x_inv = np.where(sdec > 0, np.float32(1.0) / np.where(sdec > 0, sdec, 1), 0).astype(np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        p = (blk * x_inv[:, :, None]).astype(np.float32)
+    c = np.where(np.isnan(p), np.float32(-6.0), np.minimum(np.maximum(p, -6.0), 6.0)).astype(np.float32)
+    codes = np_e2m1_encode(c).reshape(M, K)
+    xq = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    scales = np.full((nv_sf_bytes(M, K),), 0x38, np.uint8)
+    r, g = np.meshgrid(np.arange(M), np.arange(nblk), indexing="ij")
+    scales[mx_sf_offset(r, g, ncb)] = s8
+    return xq, scales
+
+
+def np_nv_decode(q: np.ndarray, sc: np.ndarray) -> np.ndarray:
+    """float64 values of NVFP4 packed codes [R, K/2] with their tiled scale grid."""
+    R, K = q.shape[0], q.shape[1] * 2
+    nblk, ncb = K // 16, (K // 16 + 3) // 4
+    codes = np.empty((R, K), np.uint8)
+    codes[:, 0::2] = q & 15
+    codes[:, 1::2] = q >> 4
+    dec = np.where(codes & 8, -1.0, 1.0) * E2M1_MAG[codes & 7].astype(np.float64)
+    r, g = np.meshgrid(np.arange(R), np.arange(nblk), indexing="ij")
+    s = e4m3_decode_lut().astype(np.float64)[sc[mx_sf_offset(r, g, ncb)]]
+    return (dec.reshape(R, nblk, 16) * s[:, :, None]).reshape(R, K)
+
+
+def np_nvfp4_gemm(xq, xs, wq, ws, bias16=None, round_out=False):
+    acc = (np_nv_decode(xq, xs) @ np_nv_decode(wq, ws).T).astype(np.float32)
     if bias16 is not None:
         acc = acc + f16_bits_to_f32(np.asarray(bias16, np.uint16))[None, :]
     if round_out:
