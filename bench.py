@@ -196,19 +196,22 @@ def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True, fmt
     """``n_sets`` independent (x, wq, ws, bias[, xq, xs]) sets of workload ``wl`` on
     the current device (weights quantized once, as offline). Set i's weight depends
     only on i, so ranks hold the same weights; activations use ``x_seed0``. ``fmt``
-    "fp8": per-token / per-channel scales; "mx": MXFP8 block scales."""
+    "fp8": per-token / per-channel scales; "mx": MXFP8 block scales; "nv": NVFP4."""
     import fp8linear_b200 as f
     from fp8linear_b200.workloads import make_weight, make_x
 
+    qw = {"fp8": f.quantize_weight, "mx": f.quantize_weight_mxfp8,
+          "nv": f.quantize_weight_nvfp4}[fmt]
+    qx = {"fp8": f.quantize_fp8, "mx": f.quantize_mxfp8, "nv": f.quantize_nvfp4}[fmt]
     sets = []
     for i in range(n_sets):
         x = make_x(wl, seed=x_seed0 + 7919 * i, gen_device="cuda")
         w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
-        wq, ws = f.quantize_weight_mxfp8(w) if fmt == "mx" else f.quantize_weight(w)
+        wq, ws = qw(w)
         del w
         s = {"x": x, "wq": wq, "ws": ws, "b": b}
         if quantize_x:
-            s["xq"], s["xs"] = f.quantize_mxfp8(x) if fmt == "mx" else f.quantize_fp8(x)
+            s["xq"], s["xs"] = qx(x)
         sets.append(s)
     return sets
 
@@ -465,8 +468,8 @@ def run_gpu(args):
 def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> dict:
     """Per-workload device times of the fused op, the GEMM alone and the quantizer
     alone: each is ``max(steps, sets)`` launches back to back in one CUDA graph over
-    rotating operand sets (inputs larger than L2), averaged per launch. ``fmt`` "mx":
-    the MXFP8 ops (mxfp8_linear, mxfp8_gemm, quantize_mxfp8) instead."""
+    rotating operand sets (inputs larger than L2), averaged per launch. ``fmt`` "mx" / "nv":
+    the MXFP8 / NVFP4 ops (mxfp8_linear, mxfp8_gemm, quantize_mxfp8 / the nvfp4 ones)."""
     import fp8linear_b200 as f
     from fp8linear_b200.workloads import WORKLOADS
 
@@ -476,7 +479,6 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
     sets = operand_sets(wl, n_sets, fmt=fmt)
     stream = torch.cuda.current_stream(dev)
     reps = max(steps, n_sets)
-    mx = fmt == "mx"
 
     def timed(call):
         for i in range(warmup):
@@ -486,17 +488,29 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
         del g
         return ms
 
-    lin_op, gemm_op, quant_op = ((f.mxfp8_linear, f.mxfp8_gemm, f.quantize_mxfp8) if mx else
-                                 (f.fp8_linear, f.fp8_gemm, f.quantize_fp8))
+    lin_op, gemm_op, quant_op = {
+        "fp8": (f.fp8_linear, f.fp8_gemm, f.quantize_fp8),
+        "mx": (f.mxfp8_linear, f.mxfp8_gemm, f.quantize_mxfp8),
+        "nv": (f.nvfp4_linear, f.nvfp4_gemm, f.quantize_nvfp4)}[fmt]
     fused = timed(lambda st: lin_op(st["x"], st["wq"], st["ws"], st["b"]))
     gemm = timed(lambda st: gemm_op(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
     quant = timed(lambda st: quant_op(st["x"]))
-    # quantizer bytes: read 2MK, write MK codes + scales (4M fp32, or M*K/32 e8m0)
-    qbytes = wl.M * 3 * wl.K + (wl.M * wl.K // 32 if mx else 4 * wl.M)
+    # quantizer bytes: read 2MK, write the codes (MK, NV MK/2) and the scales (4M fp32,
+    # MK/32 e8m0, MK/16 ue4m3)
+    mk = wl.M * wl.K
+    qbytes = {"fp8": 3 * mk + 4 * wl.M, "mx": 3 * mk + mk // 32,
+              "nv": 2 * mk + mk // 2 + mk // 16}[fmt]
     pk = peaks()
-    # bandwidth-aware roofline for the GEMM: min(tensor peak, AI x HBM)
-    ai = wl.flops / wl.gemm_bytes
-    roof = min(2.0 * pk["bf16_tflops"], ai * pk["hbm_gbs"] / 1e3)
+    # bandwidth-aware roofline for the GEMM: min(tensor peak, AI x HBM); the e4m3 forms run
+    # at 2x and e2m1 at 4x the measured bf16 rate (the nominal dense ratios), and the NVFP4
+    # operands are half the bytes (+ one scale byte per 16 elements)
+    if fmt == "nv":
+        gbytes = (wl.M + wl.N) * wl.K * 9 // 16 + 2 * wl.N + 2 * wl.M * wl.N
+        rate = 4.0
+    else:
+        gbytes, rate = wl.gemm_bytes, 2.0
+    ai = wl.flops / gbytes
+    roof = min(rate * pk["bf16_tflops"], ai * pk["hbm_gbs"] / 1e3)
     g_tf = wl.flops / (gemm * 1e-3) / 1e12
     return {"workload": name, "format": fmt, "M": wl.M, "K": wl.K, "N": wl.N, "sets": n_sets,
             "fused_us": round(fused * 1e3, 2),
@@ -690,7 +704,8 @@ def reference_gpu_timing(wl, args, fmt: str = "fp8"):
     """Device time of the reference's own compiled CUDA ops (cuBLASLt FP8 GEMM + dequant
     kernel, fp16 out, then the .to(bf16) cast Fp8Linear.forward applies), if built,
     timed like our op: launches back to back over rotating operand sets. ``fmt`` "mx":
-    its mxfp8_linear (quantize_mxfp8 + cuBLASLt VEC32_UE8M0 GEMM with bias, fp16 out)."""
+    its mxfp8_linear (quantize_mxfp8 + cuBLASLt VEC32_UE8M0 GEMM with bias, fp16 out);
+    "nv": its nvfp4_linear (quantize_nvfp4 + cuBLASLt VEC16_UE4M3 e2m1 GEMM)."""
     try:
         from oracle import build_ref
         ref = build_ref.load()
@@ -707,11 +722,12 @@ def reference_gpu_timing(wl, args, fmt: str = "fp8"):
     for i in range(n_sets):
         x = make_x(wl, seed=7919 * i, gen_device="cuda")
         w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
-        wq, ws = ref.quantize_mxfp8(w) if fmt == "mx" else ref.quantize_weight(w)
+        qw = {"fp8": ref.quantize_weight, "mx": ref.quantize_mxfp8, "nv": ref.quantize_nvfp4}[fmt]
+        wq, ws = qw(w)
         sets.append({"x": x, "wq": wq, "ws": ws, "b": b})
         del w
     stream = torch.cuda.current_stream(dev)
-    lin = ref.mxfp8_linear if fmt == "mx" else ref.fp8_linear
+    lin = {"fp8": ref.fp8_linear, "mx": ref.mxfp8_linear, "nv": ref.nvfp4_linear}[fmt]
 
     def call(st):
         return lin(st["x"], st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
@@ -761,8 +777,9 @@ def main():
                          "channels with an NCCL all-gather")
     ap.add_argument("--fused", action="store_true",
                     help="with --mode nshard: fuse the all-gather into the GEMM epilogue")
-    ap.add_argument("--format", choices=["fp8", "mx"], default="fp8",
-                    help="with --sweep: per-channel FP8 ops (default) or the MXFP8 ops")
+    ap.add_argument("--format", choices=["fp8", "mx", "nv"], default="fp8",
+                    help="with --sweep: per-channel FP8 ops (default), the MXFP8 or the "
+                         "NVFP4 ops")
     ap.add_argument("--sweep", default="",
                     help="'all' or comma-separated workloads: one JSON line of per-kernel "
                          "device times per workload (not the driver's line)")

@@ -31,6 +31,11 @@ SIGNATURES = {
     "fp8lin_mxfp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
     "fp8lin_mxfp8_linear_workspace_size": (_SZ, [_I64, _I64]),
     "fp8lin_mxfp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+    "fp8lin_nv_scale_bytes": (_SZ, [_I64, _I64]),
+    "fp8lin_quantize_nvfp4": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
+    "fp8lin_nvfp4_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
+    "fp8lin_nvfp4_linear_workspace_size": (_SZ, [_I64, _I64]),
+    "fp8lin_nvfp4_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
     "fp8lin_fp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
     "fp8lin_linear_workspace_size": (_SZ, [_I64, _I64]),
     "fp8lin_fp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
@@ -127,6 +132,47 @@ class CApi:
                                           DTYPE[out.dtype], M, N, K, workspace.data_ptr(),
                                           workspace.numel(), self._stream(x))
         self._check(rc, "fp8lin_mxfp8_linear")
+        return out
+
+    def nv_scale_bytes(self, rows: int, K: int) -> int:
+        return int(self.lib.fp8lin_nv_scale_bytes(rows, K))
+
+    def quantize_nvfp4(self, x: torch.Tensor, xq: torch.Tensor | None = None,
+                       scales: torch.Tensor | None = None):
+        M, K = x.shape
+        xq = torch.empty((M, K // 2), dtype=torch.uint8, device=x.device) if xq is None else xq
+        if scales is None:
+            scales = torch.empty((self.nv_scale_bytes(M, K),), dtype=torch.uint8, device=x.device)
+        rc = self.lib.fp8lin_quantize_nvfp4(x.data_ptr(), DTYPE[x.dtype], M, K, xq.data_ptr(),
+                                            scales.data_ptr(), self._stream(x))
+        self._check(rc, "fp8lin_quantize_nvfp4")
+        return xq, scales
+
+    def nvfp4_gemm(self, xq, x_scales, wq, w_scales, bias=None, out_dtype=torch.bfloat16,
+                   out=None):
+        M, K = xq.shape[0], xq.shape[1] * 2
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=out_dtype, device=xq.device) if out is None else out
+        rc = self.lib.fp8lin_nvfp4_gemm(xq.data_ptr(), x_scales.data_ptr(), wq.data_ptr(),
+                                        w_scales.data_ptr(), self._bias_ptr(bias),
+                                        self._bias_dtype(bias), out.data_ptr(), DTYPE[out.dtype],
+                                        M, N, K, self._stream(xq))
+        self._check(rc, "fp8lin_nvfp4_gemm")
+        return out
+
+    def nvfp4_linear(self, x, wq, w_scales, bias=None, out=None, workspace=None):
+        M, K = x.shape
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device) if out is None else out
+        need = int(self.lib.fp8lin_nvfp4_linear_workspace_size(M, K))
+        if workspace is None:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+        rc = self.lib.fp8lin_nvfp4_linear(x.data_ptr(), DTYPE[x.dtype], wq.data_ptr(),
+                                          w_scales.data_ptr(), self._bias_ptr(bias),
+                                          self._bias_dtype(bias), out.data_ptr(),
+                                          DTYPE[out.dtype], M, N, K, workspace.data_ptr(),
+                                          workspace.numel(), self._stream(x))
+        self._check(rc, "fp8lin_nvfp4_linear")
         return out
 
     def quantize_weight(self, w: torch.Tensor):

@@ -282,6 +282,104 @@ int fp8lin_mxfp8_linear(const void *x, int x_dtype, const void *wq, const void *
   return launch_gemm(a, s, true);
 }
 
+size_t fp8lin_nv_scale_bytes(int64_t rows, int64_t K) {
+  if (rows <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(nv_scale_bytes(rows, K));
+}
+
+int fp8lin_quantize_nvfp4(const void *x, int x_dtype, int64_t M, int64_t K, void *xq,
+                          void *scales, void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_nvfp4: x must be fp16 or bf16");
+  if (M < 0 || K < 0) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_nvfp4: negative size");
+  if (K % 32 != 0)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                "quantize_nvfp4: K must be a multiple of 32 for NVFP4, got " + std::to_string(K));
+  if (M == 0) return FP8LIN_OK;
+  if (K == 0) return fail(FP8LIN_ERR_UNSUPPORTED, "quantize_nvfp4: K must be positive");
+  if (!x || !xq || !scales)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "quantize_nvfp4: null pointer");
+  if (!aligned(x, 16) || !aligned(xq, 4) || !aligned(scales, 4))
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                "quantize_nvfp4: x must be 16-byte, xq and scales 4-byte aligned");
+  cudaError_t e = launch_quantize_nv(x, x_dtype, M, K, static_cast<uint8_t *>(xq),
+                                     static_cast<uint8_t *>(scales),
+                                     static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("quantize_nvfp4: launch: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
+int fp8lin_nvfp4_gemm(const void *xq, const void *x_scales, const void *wq, const void *w_scales,
+                      const void *bias, int bias_dtype, void *out, int out_dtype, int64_t M,
+                      int64_t N, int64_t K, void *stream) {
+  clear_error();
+  const float *dummy = reinterpret_cast<const float *>(16);
+  int rc = check_gemm_args(xq, dummy, wq, dummy, bias, bias_dtype, out, out_dtype, M, N, K,
+                           "nvfp4_gemm");
+  if (rc != FP8LIN_OK) return rc;
+  if (K % 32 != 0)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                "nvfp4_gemm: K must be a multiple of 32 for NVFP4, got " + std::to_string(K));
+  if (M == 0 || N == 0) return FP8LIN_OK;
+  if (!x_scales || !w_scales) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "nvfp4_gemm: null scales");
+  if (!aligned(x_scales, 16) || !aligned(w_scales, 16))
+    return fail(FP8LIN_ERR_UNSUPPORTED, "nvfp4_gemm: scale grids must be 16-byte aligned");
+  GemmArgs a{static_cast<const uint8_t *>(xq), nullptr, static_cast<const uint8_t *>(wq),
+             nullptr, bias, bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  a.mx = true;
+  a.nv = true;
+  a.xsf = static_cast<const uint8_t *>(x_scales);
+  a.wsf = static_cast<const uint8_t *>(w_scales);
+  return launch_gemm(a, static_cast<cudaStream_t>(stream), false);
+}
+
+size_t fp8lin_nvfp4_linear_workspace_size(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  return round_up(static_cast<size_t>(M) * static_cast<size_t>(K) / 2, kWsAlign) +
+         round_up(static_cast<size_t>(nv_scale_bytes(M, K)), kWsAlign);
+}
+
+int fp8lin_nvfp4_linear(const void *x, int x_dtype, const void *wq, const void *w_scales,
+                        const void *bias, int bias_dtype, void *out, int out_dtype, int64_t M,
+                        int64_t N, int64_t K, void *workspace, size_t workspace_bytes,
+                        void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "nvfp4_linear: x must be fp16 or bf16");
+  const float *dummy = reinterpret_cast<const float *>(16);
+  int rc = check_gemm_args(reinterpret_cast<const void *>(16), dummy, wq, dummy, bias, bias_dtype,
+                           out, out_dtype, M, N, K, "nvfp4_linear");
+  if (rc != FP8LIN_OK) return rc;
+  if (K % 32 != 0)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                "nvfp4_linear: K must be a multiple of 32 for NVFP4, got " + std::to_string(K));
+  if (M == 0 || N == 0) return FP8LIN_OK;
+  if (!x || !w_scales) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "nvfp4_linear: null pointer");
+  if (!aligned(x, 16) || !aligned(w_scales, 16))
+    return fail(FP8LIN_ERR_UNSUPPORTED, "nvfp4_linear: x and w_scales must be 16-byte aligned");
+  const size_t need = fp8lin_nvfp4_linear_workspace_size(M, K);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, kWsAlign))
+    return fail(FP8LIN_ERR_WORKSPACE, "nvfp4_linear: workspace of " + std::to_string(need) +
+                                          " bytes (256-byte aligned) required, got " +
+                                          std::to_string(workspace_bytes));
+  uint8_t *xq = static_cast<uint8_t *>(workspace);
+  uint8_t *xsf = xq + round_up(static_cast<size_t>(M) * static_cast<size_t>(K) / 2, kWsAlign);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_quantize_nv(x, x_dtype, M, K, xq, xsf, s, true);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("nvfp4_linear: quantize launch: ") +
+                                     cudaGetErrorString(e));
+  GemmArgs a{xq, nullptr, static_cast<const uint8_t *>(wq), nullptr, bias,
+             bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  a.mx = true;
+  a.nv = true;
+  a.xsf = xsf;
+  a.wsf = static_cast<const uint8_t *>(w_scales);
+  return launch_gemm(a, s, true);
+}
+
 int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, const float *w_scale,
                                 const void *bias, int bias_dtype, void *const *outs, int n_outs,
                                 int out_dtype, int64_t M, int64_t N, int64_t K, int64_t ldo,

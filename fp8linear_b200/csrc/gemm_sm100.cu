@@ -64,23 +64,34 @@ constexpr uint32_t EPI_BUF = 32 * EPI_COLS * 2;  // 4 KB: 32 rows x 64 cols x 2 
 constexpr uint32_t PAR_BYTES = 2 * BN * 4;       // per epilogue warp: w_scale + bias of a tile
 constexpr uint32_t RING_BYTES = 160 * 1024;      // operand ring (both shapes)
 
-// MX = true: the MXFP8 (block-scaled) form. Each stage also carries the e8m0 scale tiles
-// of the K-block: one 512-byte tile for this CTA's 128 rows of A and two for the tile's
-// 256 rows of B (every CTA of a pair holds the scales of all 256 B rows, which the MMA
-// reads for its N = 256). Before a K-block's MMAs they are copied into TMEM
-// (tcgen05.cp .32x128b.warpx4, 4 columns per tile) next to the accumulators. To make room,
-// the two accumulators overlap by one epilogue chunk: accumulator 0 = columns 0-255,
-// accumulator 1 = columns 192-447, scale factors at 448-459; the epilogue reads the shared
-// chunk first and releases it before the rest (bar_tovl).
-template <int CG, bool MX = false>
+// Operand formats (template parameter F):
+//   kFmtE4M3  per-token x per-channel e4m3 (scales applied in the epilogue);
+//   kFmtMX    MXFP8: e4m3 codes, one e8m0 scale per 32 K-elements of every row;
+//   kFmtNV    NVFP4: e2m1 codes packed two per byte, one ue4m3 scale per 16 K-elements.
+// Both block-scaled forms keep the operand pipeline byte for byte (a K-block is 128 bytes of
+// a row: 128 e4m3 or 256 e2m1 elements, four MMAs of 32 bytes) and add the scale tiles of
+// the K-block to each stage, in the tiled layout of the quantizers: 512-byte tiles of 128
+// rows x 4 scales. MX: one tile per K-block for this CTA's 128 rows of A and two for the
+// tile's 256 rows of B; NV: four and eight (every CTA of a pair holds the scales of all 256
+// B rows, which the MMA reads for its N = 256). Before a K-block's MMAs they are copied into
+// TMEM (tcgen05.cp .32x128b.warpx4, 4 columns per tile) next to the accumulators. To make
+// room, the two accumulators overlap by one epilogue chunk: accumulator 0 = columns 0-255,
+// accumulator 1 = columns 192-447, scale factors from column 448 (MX 12 columns, NV 48);
+// the epilogue reads the shared chunk first and releases it before the rest (bar_tovl).
+enum : int { kFmtE4M3 = 0, kFmtMX = 1, kFmtNV = 2 };
+
+template <int CG, int F = kFmtE4M3>
 struct Cfg {
+  static constexpr bool MX = F != kFmtE4M3;                    // block-scaled (MX or NV)
+  static constexpr bool NV = F == kFmtNV;
+  static constexpr int SF_TILES = NV ? 4 : 1;                  // scale tiles per K-block, row block
   static constexpr int B_ROWS = BN / CG;                       // B rows this CTA loads
   static constexpr uint32_t B_STAGE = B_ROWS * BK;             // 32 KB (CG 1) / 16 KB (CG 2)
-  static constexpr uint32_t SFA_STAGE = MX ? 512u : 0u;        // A scales of the K-block
-  static constexpr uint32_t SFB_STAGE = MX ? 1024u : 0u;       // B scales, all 256 rows
+  static constexpr uint32_t SFA_STAGE = MX ? 512u * SF_TILES : 0u;   // A scales of the K-block
+  static constexpr uint32_t SFB_STAGE = MX ? 1024u * SF_TILES : 0u;  // B scales, all 256 rows
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE + SFA_STAGE + SFB_STAGE;
   static constexpr uint32_t RING = MX ? 168u * 1024u : RING_BYTES;
-  static constexpr int STAGES = RING / STAGE;                  // 3 / 5 (MX: 3 / 5)
+  static constexpr int STAGES = RING / STAGE;  // 3 / 5 (MX: 3 / 5, NV: 3 / 4)
   static constexpr uint32_t TX_BYTES = CG * STAGE;             // bytes landing per stage
   static constexpr int TILE_M = BM * CG;
   static constexpr uint32_t OFF_A = 0;
@@ -96,14 +107,15 @@ struct Cfg {
   static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
   static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + base alignment slack
   static constexpr uint32_t IDESC = ptx::idesc_e4m3_f32(TILE_M, BN);
-  static constexpr uint32_t IDESC_MX = ptx::idesc_mx_e4m3(TILE_M, BN, 0);
+  static constexpr uint32_t IDESC_MX =
+      NV ? ptx::idesc_nv_e2m1(TILE_M, BN) : ptx::idesc_mx_e4m3(TILE_M, BN, 0);
   static constexpr uint32_t ACC1_COL = MX ? BN - EPI_COLS : BN;  // accumulator 1's column
-  static constexpr uint32_t SFA_COL = 2 * BN - EPI_COLS;          // MX scale factors
-  static constexpr uint32_t SFB_COL = SFA_COL + 4;
+  static constexpr uint32_t SFA_COL = 2 * BN - EPI_COLS;          // block scale factors:
+  static constexpr uint32_t SFB_COL = SFA_COL + 4 * SF_TILES;     // A 4/tile, B 8/tile
   static_assert(STAGES * STAGE <= RING, "ring");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(OFF_B % 1024 == 0 && OFF_EPI % 1024 == 0, "swizzle atoms need 1024 B alignment");
-  static_assert(!MX || SFB_COL + 8 <= TMEM_COLS, "TMEM budget");
+  static_assert(!MX || SFB_COL + 8 * SF_TILES <= TMEM_COLS, "TMEM budget");
 };
 
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
@@ -117,7 +129,7 @@ struct Params {
   int out_dtype;
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
-  int ncb;           // MX: scale tiles per 128-row block (ceil(K / 128))
+  int ncb;           // MX / NV: scale tiles per 128-row block (ceil(K / 128) / ceil(K / 64))
   int n_fastest;     // tile order
   int direct_store;  // rows not 16-byte multiples / unaligned: no TMA store
   void *out;         // output base (direct stores)
@@ -154,14 +166,16 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
   }
 }
 
-template <int CG, bool MX>
+template <int CG, int F>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_out,
                     const __grid_constant__ CUtensorMap tmap_sfa,
                     const __grid_constant__ CUtensorMap tmap_sfb, const Params p) {
-  using C = Cfg<CG, MX>;
+  using C = Cfg<CG, F>;
+  constexpr bool MX = C::MX;
+  constexpr bool NV = C::NV;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -240,10 +254,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = bar_full + 8 * stage;
           const uint32_t dst_a = sbase + C::OFF_A + stage * A_STAGE;
           const uint32_t dst_b = sbase + C::OFF_B + stage * C::B_STAGE;
-          // MX scale tiles of this K-block: row (128-row block * ncb + kb) of the tiled
-          // scale arrays; blocks past the end read as zero (rows that are never stored).
-          const int sfa_row = (a_row >> 7) * p.ncb + kb;
-          const int sfb_row = ((nt * BN) >> 7) * p.ncb + kb;
+          // block-scale tiles of this K-block: tiles kb * SF_TILES .. of a 128-row block
+          // (coordinates tile, row block of the [row blocks][ncb][512 B] grids); tiles and
+          // row blocks past the end read as zero (scales of codes that are zero fill).
+          const int sf_tile = kb * C::SF_TILES;
+          const int sfa_rb = a_row >> 7;
+          const int sfb_rb = (nt * BN) >> 7;
           const uint32_t dst_sfa = sbase + C::OFF_SFA + stage * C::SFA_STAGE;
           const uint32_t dst_sfb = sbase + C::OFF_SFB + stage * C::SFB_STAGE;
           if constexpr (CG == 1) {
@@ -251,9 +267,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ptx::tma_load_2d(dst_a, &tmap_a, kb * BK, a_row, fb);
             ptx::tma_load_2d(dst_b, &tmap_b, kb * BK, b_row, fb);
             if constexpr (MX) {
-              ptx::tma_load_2d(dst_sfa, &tmap_sfa, 0, sfa_row, fb);
-              ptx::tma_load_2d(dst_sfb, &tmap_sfb, 0, sfb_row, fb);
-              ptx::tma_load_2d(dst_sfb + 512, &tmap_sfb, 0, sfb_row + p.ncb, fb);
+              ptx::tma_load_3d(dst_sfa, &tmap_sfa, 0, sf_tile, sfa_rb, fb);
+              ptx::tma_load_3d(dst_sfb, &tmap_sfb, 0, sf_tile, sfb_rb, fb);
+              ptx::tma_load_3d(dst_sfb + C::SFB_STAGE / 2, &tmap_sfb, 0, sf_tile, sfb_rb + 1, fb);
             }
           } else {
             // Both CTAs' bytes complete the leader's barrier; only the leader arms it.
@@ -262,9 +278,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ptx::tma_load_2d_pair(dst_a, &tmap_a, kb * BK, a_row, fb_leader);
             ptx::tma_load_2d_pair(dst_b, &tmap_b, kb * BK, b_row, fb_leader);
             if constexpr (MX) {
-              ptx::tma_load_2d_pair(dst_sfa, &tmap_sfa, 0, sfa_row, fb_leader);
-              ptx::tma_load_2d_pair(dst_sfb, &tmap_sfb, 0, sfb_row, fb_leader);
-              ptx::tma_load_2d_pair(dst_sfb + 512, &tmap_sfb, 0, sfb_row + p.ncb, fb_leader);
+              ptx::tma_load_3d_pair(dst_sfa, &tmap_sfa, 0, sf_tile, sfa_rb, fb_leader);
+              ptx::tma_load_3d_pair(dst_sfb, &tmap_sfb, 0, sf_tile, sfb_rb, fb_leader);
+              ptx::tma_load_3d_pair(dst_sfb + C::SFB_STAGE / 2, &tmap_sfb, 0, sf_tile,
+                                    sfb_rb + 1, fb_leader);
             }
           }
           ++issued;
@@ -321,20 +338,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t adesc = ptx::sw128_kmajor_desc(sbase + C::OFF_A + stage * A_STAGE);
           const uint64_t bdesc = ptx::sw128_kmajor_desc(sbase + C::OFF_B + stage * C::B_STAGE);
           if constexpr (MX) {
-            // this K-block's scales into TMEM, ahead of its MMAs in the same pipe
+            // this K-block's scales into TMEM, ahead of its MMAs in the same pipe: tile j
+            // of A to columns SFA_COL + 4j, tile j of B rows 0-127 / 128-255 to
+            // SFB_COL + 8j / + 8j + 4
             const uint32_t sfa_s = sbase + C::OFF_SFA + stage * C::SFA_STAGE;
             const uint32_t sfb_s = sbase + C::OFF_SFB + stage * C::SFB_STAGE;
-            ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFA_COL, ptx::sf_block_desc(sfa_s));
-            ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFB_COL, ptx::sf_block_desc(sfb_s));
-            ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFB_COL + 4,
-                                        ptx::sf_block_desc(sfb_s + 512));
+#pragma unroll
+            for (int j = 0; j < C::SF_TILES; ++j) {
+              ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFA_COL + 4 * j,
+                                          ptx::sf_block_desc(sfa_s + 512 * j));
+              ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFB_COL + 8 * j,
+                                          ptx::sf_block_desc(sfb_s + 512 * j));
+              ptx::tmem_cp_32x128b_x4<CG>(tmem_base + C::SFB_COL + 8 * j + 4,
+                                          ptx::sf_block_desc(sfb_s + C::SFB_STAGE / 2 + 512 * j));
+            }
           }
 #pragma unroll
           for (int kk = 0; kk < BK / UMMA_K; ++kk) {
             // advance the start address by kk*32 bytes inside the swizzle atom
             const uint64_t koff = static_cast<uint64_t>((kk * UMMA_K) >> 4);
             const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
-            if constexpr (MX) {
+            if constexpr (NV) {
+              // 64 elements = four 16-element blocks = the whole scale word of tile kk
+              ptx::mma_nvf4<CG>(d_tmem, adesc + koff, bdesc + koff, C::IDESC_MX,
+                                tmem_base + C::SFA_COL + 4 * kk,
+                                tmem_base + C::SFB_COL + 8 * kk, accumulate);
+            } else if constexpr (MX) {
               // scale byte kk of each 32-bit scale word: the kk-th 32-element block
               const uint32_t sfid = static_cast<uint32_t>(kk) << 30;
               ptx::mma_mxf8f6f4<CG>(d_tmem, adesc + koff, bdesc + koff,
@@ -569,6 +598,31 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// [outer][mid][inner] array with byte strides mid_bytes / outer_bytes, box
+// box_inner x box_mid x 1, no swizzle: the block-scale grids as
+// [128-row blocks][scale tiles][128 words of 4 scales].
+bool make_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner,
+                  uint64_t mid, uint64_t outer, uint64_t mid_bytes, uint64_t outer_bytes,
+                  uint32_t box_inner, uint32_t box_mid, std::string *err) {
+  auto fn = encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is unavailable (driver entry point query failed)";
+    return false;
+  }
+  cuuint64_t dims[3] = {inner, mid, outer};
+  cuuint64_t strides[2] = {mid_bytes, outer_bytes};
+  cuuint32_t box[3] = {box_inner, box_mid, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
 bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner,
                   uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                   CUtensorMapSwizzle swizzle, std::string *err) {
@@ -598,7 +652,7 @@ struct LaunchInfo {
   int max_groups = 0;
 };
 
-template <int CG, bool MX>
+template <int CG, int F>
 LaunchInfo &launch_info(int device, int sm_count) {
   static LaunchInfo info[64];
   static std::mutex mu;
@@ -606,14 +660,14 @@ LaunchInfo &launch_info(int device, int sm_count) {
   LaunchInfo &li = info[device & 63];
   if (!li.ready) {
     li.ready = true;
-    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(Cfg<CG, MX>::SMEM_BYTES));
+    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(Cfg<CG, F>::SMEM_BYTES));
     li.max_groups = sm_count / CG;
     if (li.err == cudaSuccess && CG == 2) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(sm_count);
       cfg.blockDim = dim3(NUM_THREADS);
-      cfg.dynamicSmemBytes = Cfg<CG, MX>::SMEM_BYTES;
+      cfg.dynamicSmemBytes = Cfg<CG, F>::SMEM_BYTES;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = CG;
@@ -622,7 +676,7 @@ LaunchInfo &launch_info(int device, int sm_count) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG, MX>, &cfg);
+      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG, F>, &cfg);
       if (li.err == cudaSuccess) li.max_groups = std::min(li.max_groups, clusters);
       if (li.err == cudaSuccess && li.max_groups < 1) li.err = cudaErrorInvalidConfiguration;
     }
@@ -630,31 +684,37 @@ LaunchInfo &launch_info(int device, int sm_count) {
   return li;
 }
 
-template <int CG, bool MX>
+template <int CG, int F>
 int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
-  using C = Cfg<CG, MX>;
+  using C = Cfg<CG, F>;
+  constexpr bool MX = C::MX;
+  const char *name = C::NV ? "nvfp4_gemm: " : MX ? "mxfp8_gemm: " : "fp8_gemm: ";
   std::string err;
   CUtensorMap ta, tb, tout, tsfa, tsfb;
-  const int64_t ncb = (a.K + BK - 1) / BK;  // MX: scale tiles per 128-row block
+  // bytes of a row of codes (NV: two e2m1 codes per byte) and scale tiles per 128-row
+  // block (4 scales of 32 (MX) or 16 (NV) elements per tile)
+  const int64_t kbytes = C::NV ? a.K / 2 : a.K;
+  const int64_t ncb = C::NV ? (a.K / 16 + 3) / 4 : (a.K / 32 + 3) / 4;
   if constexpr (MX) {
-    // the tiled e8m0 scale grids as [tiles, 128] arrays of 32-bit words: one row per
-    // 512-byte tile (128 rows x 4 scales), row = 128-row block * ncb + K-block
-    const uint64_t tiles_a = static_cast<uint64_t>((a.M + 127) / 128 * ncb);
-    const uint64_t tiles_b = static_cast<uint64_t>((a.N + 127) / 128 * ncb);
-    if (!make_tmap_2d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.xsf, 128, tiles_a, 512, 128, 1,
-                      CU_TENSOR_MAP_SWIZZLE_NONE, &err) ||
-        !make_tmap_2d(&tsfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.wsf, 128, tiles_b, 512, 128, 1,
-                      CU_TENSOR_MAP_SWIZZLE_NONE, &err)) {
-      set_error("mxfp8_gemm: " + err);
+    // the tiled scale grids as [row blocks][ncb tiles][128 words]; a box is the
+    // SF_TILES tiles of one K-block of one row block
+    const uint64_t rb_a = static_cast<uint64_t>((a.M + 127) / 128);
+    const uint64_t rb_b = static_cast<uint64_t>((a.N + 127) / 128);
+    const uint64_t nt = static_cast<uint64_t>(ncb);
+    if (!make_tmap_3d(&tsfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.xsf, 128, nt, rb_a, 512, nt * 512,
+                      128, C::SF_TILES, &err) ||
+        !make_tmap_3d(&tsfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.wsf, 128, nt, rb_b, 512, nt * 512,
+                      128, C::SF_TILES, &err)) {
+      set_error(name + err);
       return 4;
     }
   }
   const int64_t ldo = a.ldo > 0 ? a.ldo : a.N;
   const bool direct = (a.N % 8) != 0 || (ldo % 8) != 0 ||
                       (reinterpret_cast<uintptr_t>(a.out) % 16) != 0;
-  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.xq, a.K, a.M, a.K, BK, BM,
+  if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.xq, kbytes, a.M, kbytes, BK, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B, &err) ||
-      !make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wq, a.K, a.N, a.K, BK, C::B_ROWS,
+      !make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.wq, kbytes, a.N, kbytes, BK, C::B_ROWS,
                     CU_TENSOR_MAP_SWIZZLE_128B, &err) ||
       // rows of N bf16 are a 16-byte multiple only for N % 8 == 0: otherwise the
       // epilogue stores directly and the (unused) output map is a placeholder over xq
@@ -665,7 +725,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
                     direct ? 8 : EPI_COLS, direct ? 1 : 32, direct ? CU_TENSOR_MAP_SWIZZLE_NONE
                                                              : CU_TENSOR_MAP_SWIZZLE_128B,
                     &err)) {
-    set_error("fp8_gemm: " + err);
+    set_error(name + err);
     return 4;
   }
   Params p;
@@ -679,7 +739,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   p.K = static_cast<int>(a.K);
   p.m_tiles = static_cast<int>((a.M + C::TILE_M - 1) / C::TILE_M);
   p.n_tiles = static_cast<int>((a.N + BN - 1) / BN);
-  p.k_blocks = static_cast<int>((a.K + BK - 1) / BK);
+  p.k_blocks = static_cast<int>((kbytes + BK - 1) / BK);
   p.ncb = static_cast<int>(ncb);
   p.n_fastest = a.M >= a.N ? 1 : 0;
   p.direct_store = direct ? 1 : 0;
@@ -698,7 +758,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
     set_error("fp8_gemm: too many output tiles");
     return 2;
   }
-  LaunchInfo &li = launch_info<CG, MX>(dev.device, dev.sm_count);
+  LaunchInfo &li = launch_info<CG, F>(dev.device, dev.sm_count);
   if (li.err != cudaSuccess) {
     set_error(std::string("fp8_gemm: kernel setup: ") + cudaGetErrorString(li.err));
     return 4;
@@ -730,7 +790,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
     tsfa = ta;
     tsfb = ta;
   }
-  cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, MX>, ta, tb, tout, tsfa, tsfb, p);
+  cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, F>, ta, tb, tout, tsfa, tsfb, p);
   if (ce != cudaSuccess) {
     set_error(std::string("fp8_gemm: launch failed: ") + cudaGetErrorString(ce));
     return 4;
@@ -760,20 +820,24 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     set_error("fp8_gemm: dimensions must fit in int32 and at most 7 peers");
     return 2;
   }
-  // MXFP8: single CTAs with 128-row tiles for M <= 128, CTA pairs otherwise.
+  // MXFP8 / NVFP4: single CTAs with 128-row tiles for M <= 128, CTA pairs otherwise.
   if (a.mx) {
     if (a.n_peers != 0) {
-      set_error("mxfp8_gemm: peer outputs are not supported");
+      set_error("block-scaled gemm: peer outputs are not supported");
       return 2;
     }
-    if (a.M <= gemm::BM) return gemm::launch_shape<1, true>(a, dev, stream, pdl);
-    return gemm::launch_shape<2, true>(a, dev, stream, pdl);
+    if (a.nv) {
+      if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtNV>(a, dev, stream, pdl);
+      return gemm::launch_shape<2, gemm::kFmtNV>(a, dev, stream, pdl);
+    }
+    if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtMX>(a, dev, stream, pdl);
+    return gemm::launch_shape<2, gemm::kFmtMX>(a, dev, stream, pdl);
   }
   // Few tokens: stream the weights with swap-AB split-K tiles. Otherwise CTA pairs with
   // 256-row tiles (or single CTAs with 128-row tiles for peer outputs at M <= 128).
   if (a.M <= gemm::BM && a.n_peers == 0) return launch_gemm_small(a, stream, pdl);
-  if (a.M <= gemm::BM) return gemm::launch_shape<1, false>(a, dev, stream, pdl);
-  return gemm::launch_shape<2, false>(a, dev, stream, pdl);
+  if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtE4M3>(a, dev, stream, pdl);
+  return gemm::launch_shape<2, gemm::kFmtE4M3>(a, dev, stream, pdl);
 }
 
 namespace {

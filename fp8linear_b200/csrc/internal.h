@@ -41,6 +41,14 @@ cudaError_t launch_quantize_mx(const void *x, int dtype, int64_t M, int64_t K, u
 inline int64_t mx_scale_bytes(int64_t rows, int64_t K) {
   return (rows + 127) / 128 * ((K / 32 + 3) / 4) * 512;
 }
+// NVFP4 block quantization (per 16 elements: e4m3 scale, e2m1 codes packed two per byte
+// into xq [M, K/2]); scale grid of nv_scale_bytes(M, K) written whole. K % 32 == 0, x
+// 16-byte aligned, xq and scales 4-byte aligned.
+cudaError_t launch_quantize_nv(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                               uint8_t *scales, cudaStream_t stream, bool trigger_dependents);
+inline int64_t nv_scale_bytes(int64_t rows, int64_t K) {
+  return (rows + 127) / 128 * ((K / 16 + 3) / 4) * 512;
+}
 // Reads (and optionally clears) the quantizer watchdog bits (8) of the current device.
 cudaError_t read_quant_status(unsigned int *bits, bool clear);
 // Per-channel weight quantization (ATen semantics of the reference's quantize_weight).
@@ -65,9 +73,11 @@ struct GemmArgs {
   // same layout as `out`), straight from the epilogue.
   int n_peers = 0;
   void *const *peers = nullptr;
-  // MXFP8 (block-scaled) form: xs/ws unused; xsf/wsf are the tiled e8m0 scale grids of
-  // xq and wq (mx_scale_bytes(M, K) / mx_scale_bytes(N, K), 16-byte aligned).
+  // Block-scaled forms: xs/ws unused; xsf/wsf are the tiled scale grids of xq and wq,
+  // 16-byte aligned. mx alone: MXFP8 (e8m0 grids of mx_scale_bytes(M or N, K)); mx and nv:
+  // NVFP4 (xq [M, K/2] / wq [N, K/2] packed e2m1, ue4m3 grids of nv_scale_bytes).
   bool mx = false;
+  bool nv = false;
   const uint8_t *xsf = nullptr;
   const uint8_t *wsf = nullptr;
 };

@@ -108,6 +108,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int3
       : "memory");
 }
 
+// 3-D form (x innermost); same completion rules as tma_load_2d.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, int32_t x, int32_t y,
+                                            int32_t z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
 // Brings the box at (x, y) of a tensor into L2 without writing shared memory or
 // signalling any barrier (no cluster multicast). Coordinates follow the load's rules.
 __device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int32_t x, int32_t y) {
@@ -177,6 +187,16 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap,
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// 3-D form of tma_load_2d_pair.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void *tmap, int32_t x,
+                                                 int32_t y, int32_t z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
 
@@ -308,6 +328,31 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc, u
         : "memory");
 }
 
+// Block-scaled NVFP4 form (kind::mxf4nvf4, 16-element blocks, scale_vec::4X): A and B are
+// packed e2m1 (two per byte, K = 64 elements = 32 bytes per MMA), each row carrying four
+// ue4m3 scales per MMA: the whole 32-bit word of TMEM at `sfa` / `sfb`.
+template <int CG>
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                         uint32_t accumulate) {
+  if constexpr (CG == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, "
+        "[%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, "
+        "[%5], [%6], p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
 // Copy a 32-row x 128-bit block of scale factors from shared memory (descriptor) into
 // TMEM at `taddr`, broadcast to all four 32-lane quarters (.32x128b.warpx4): lane
 // 32w + i receives row i. CG = 2: issued by the leader, each CTA copying its own
@@ -427,6 +472,14 @@ __device__ __forceinline__ uint64_t sf_block_desc(uint32_t smem_addr) {
 __host__ __device__ constexpr uint32_t idesc_mx_e4m3(int m, int n, uint32_t sf_id) {
   return ((sf_id & 3u) << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) |
          (static_cast<uint32_t>(m >> 4) << 24) | ((sf_id & 3u) << 29);
+}
+
+// Instruction descriptor for kind::mxf4nvf4.block_scale: A/B e2m1 (format 1, bits 7-9 and
+// 10-11), both K-major, N>>3 in bits 17-22, scale type ue4m3 (bit 23 = 0), M>>4 in bits
+// 24-28, scale-factor ids 0 (a 4X scale vector uses the whole word). D is fp32.
+__host__ __device__ constexpr uint32_t idesc_nv_e2m1(int m, int n) {
+  return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // Instruction descriptor for kind::f8f6f4: D f32 (bits 4-5 = 1), A/B e4m3 (format 0),

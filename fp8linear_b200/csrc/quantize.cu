@@ -654,6 +654,107 @@ __global__ void __launch_bounds__(32 * kMxWarps) quant_mx_kernel(
   }
 }
 
+// ---------------------------------------------------------------- NVFP4 block quantizer
+//
+// Replaces quant_nvfp4_kernel (csrc/quantize.cu:157-194 of the reference): per 16-element
+// block, an e4m3 scale and e2m1 codes packed two per byte (element 2j in the low nibble),
+// the scales in the same tiled layout (K/16 scale columns).
+//   amax  = fmaxf-reduce |x| over the block (NaN ignored unless all NaN)
+//   s     = fminf(amax * fl(1/6), 448); s8 = e4m3_satfinite(s); sdec = value of s8
+//   x_inv = sdec > 0 ? 1 / sdec : 0   (IEEE divide)
+//   code  = e2m1(fminf(fmaxf(x * x_inv, -6), 6)): sign bit 8 when negative, magnitude by
+//           the thresholds 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5 (ties go up)
+// Lane l holds 8 consecutive elements of vector i (16 bytes): a block is 2 lanes, a
+// 4-block group of scales (one 32-bit word of the layout) is 8 lanes. Padding scales are
+// 0x38 (e4m3 1.0), written by the kernel.
+__device__ __forceinline__ uint32_t e2m1_code(float v) {
+  const uint32_t sgn = v < 0.0f ? 8u : 0u;
+  const float a = fabsf(v);
+  const uint32_t c = a < 0.25f ? 0u : a < 0.75f ? 1u : a < 1.25f ? 2u : a < 1.75f ? 3u
+                   : a < 2.5f  ? 4u : a < 3.5f  ? 5u : a < 5.0f  ? 6u : 7u;
+  return sgn | c;
+}
+
+// value of a non-negative e4m3 code (exact)
+__device__ __forceinline__ float e4m3_pos_value(uint32_t b) {
+  const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+  return e ? __uint_as_float(((e + 120u) << 23) | (m << 20))
+           : __fmul_rn(static_cast<float>(m), 0.001953125f);  // m * 2^-9
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * kMxWarps) quant_nv_kernel(
+    const T *__restrict__ x, uint8_t *__restrict__ xq, uint8_t *__restrict__ sf, int64_t M,
+    int K, int64_t rows_pad, int segs, int ncb, int trigger) {
+  if (trigger) ptx::grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * kMxWarps + (threadIdx.x >> 5);
+  const int64_t row = wid / segs;
+  if (row >= rows_pad) return;  // warp-uniform
+  const int seg = static_cast<int>(wid - row * segs);
+  const int nblk = K >> 4;
+  const bool row_live = row < M;
+  const int e0 = seg * kMxSeg;
+  const T *xr = x + (row_live ? row : 0) * static_cast<int64_t>(K);
+  uint4 v[kMxVecs];
+#pragma unroll
+  for (int i = 0; i < kMxVecs; ++i) {
+    const int el = e0 + (i * 32 + lane) * 8;
+    v[i] = (row_live && el < K) ? ld_stream_v4(xr + el) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  const int64_t sf_row = (row >> 7) * static_cast<int64_t>(ncb) * 512 + (row & 31) * 16 +
+                         ((row & 127) >> 5) * 4;
+  const float inv6 = 1.0f / 6.0f;
+#pragma unroll
+  for (int i = 0; i < kMxVecs; ++i) {
+    const int el = e0 + (i * 32 + lane) * 8;
+    const int g = el >> 4;  // this lane's 16-element block
+    const bool live = row_live && g < nblk;
+    float f[8];
+    In<T>::unpack8(v[i], f);
+    float amax = fabsf(f[0]);
+#pragma unroll
+    for (int e = 1; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float sc = fminf(__fmul_rn(amax, inv6), kE4M3Max);
+    const uint32_t s8 = live ? static_cast<uint32_t>(ptx::cvt_e4m3x2(sc, 0.0f) & 0xFFu) : 0x38u;
+    // the scales of blocks g .. g+3 from lanes l, l+2, l+4, l+6 (l = 0, 8, 16, 24)
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, s8, 2);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, s8, 4);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, s8, 6);
+    const int grp = g >> 2;
+    if ((lane & 7) == 0 && grp < ncb)
+      *reinterpret_cast<uint32_t *>(sf + sf_row + static_cast<int64_t>(grp) * 512) =
+          s8 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (live) {
+      const float sdec = e4m3_pos_value(s8);
+      const float x_inv = sdec > 0.0f ? __fdiv_rn(1.0f, sdec) : 0.0f;
+      uint32_t packed = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float q = fminf(fmaxf(__fmul_rn(f[e], x_inv), -6.0f), 6.0f);
+        packed |= e2m1_code(q) << (4 * e);
+      }
+      *reinterpret_cast<uint32_t *>(xq + (row * static_cast<int64_t>(K) + el) / 2) = packed;
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_nv_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, uint8_t *sf,
+                            cudaStream_t stream, bool trigger) {
+  const int64_t rows_pad = (M + 127) / 128 * 128;
+  const int segs = static_cast<int>((K + kMxSeg - 1) / kMxSeg);
+  const int ncb = static_cast<int>((K / 16 + 3) / 4);
+  const int64_t warps = rows_pad * segs;
+  const int64_t blocks = (warps + kMxWarps - 1) / kMxWarps;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  quant_nv_kernel<T><<<static_cast<unsigned>(blocks), 32 * kMxWarps, 0, stream>>>(
+      reinterpret_cast<const T *>(x), xq, sf, M, static_cast<int>(K), rows_pad, segs, ncb,
+      trigger ? 1 : 0);
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_mx_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, uint8_t *sf,
                             cudaStream_t stream, bool trigger) {
@@ -685,6 +786,14 @@ cudaError_t launch_quantize_mx(const void *x, int dtype, int64_t M, int64_t K, u
   if (dtype == kBF16)
     return launch_mx_typed<__nv_bfloat16>(x, M, K, xq, scales, stream, trigger_dependents);
   return launch_mx_typed<__half>(x, M, K, xq, scales, stream, trigger_dependents);
+}
+
+cudaError_t launch_quantize_nv(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
+                               uint8_t *scales, cudaStream_t stream, bool trigger_dependents) {
+  if (M == 0) return cudaSuccess;
+  if (dtype == kBF16)
+    return launch_nv_typed<__nv_bfloat16>(x, M, K, xq, scales, stream, trigger_dependents);
+  return launch_nv_typed<__half>(x, M, K, xq, scales, stream, trigger_dependents);
 }
 
 cudaError_t read_quant_status(unsigned int *bits, bool clear) {

@@ -12,10 +12,9 @@
 // (csrc/fp8_gemm.cu:163). Here fp8_linear returns x's dtype (bf16 for bf16 input,
 // fp16 for fp16 input) and fp8_gemm returns bf16.
 //
-// The reference's MXFP8 schemas (torch-ext/torch_binding.cpp:30-46) are implemented
-// (block-scaled tcgen05 GEMM; mxfp8_gemm returns bf16, mxfp8_linear x's dtype); its NVFP4
-// schemas (:48-65) are registered so that code probing for them finds them, and raise a
-// clear error.
+// The reference's MXFP8 and NVFP4 schemas (torch-ext/torch_binding.cpp:30-65) are
+// implemented the same way (block-scaled tcgen05 GEMMs; mxfp8_gemm / nvfp4_gemm return
+// bf16, mxfp8_linear / nvfp4_linear x's dtype).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
@@ -28,6 +27,8 @@
 namespace {
 
 at::Tensor mxfp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scales,
+                        std::optional<at::Tensor> bias);
+at::Tensor nvfp4_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scales,
                         std::optional<at::Tensor> bias);
 
 int dtype_code(at::ScalarType t) {
@@ -75,19 +76,17 @@ std::tuple<at::Tensor, at::Tensor> quantize_fp8(at::Tensor x) {
 }
 
 std::tuple<at::Tensor, at::Tensor> quantize_mxfp8(at::Tensor x);
+std::tuple<at::Tensor, at::Tensor> quantize_nvfp4(at::Tensor x);
 
-// Per-channel by default; with FP8LINEAR_USE_MX set on an sm_100 device the weight is
-// quantized to MXFP8 instead (the reference's opt-in, csrc/quantize.cu:344-357; fp32
-// weights go through bf16 first). FP8LINEAR_USE_NVFP4 is not provided and raises.
+// Per-channel by default; on an sm_100 device FP8LINEAR_USE_NVFP4 selects NVFP4 weights
+// and, failing that, FP8LINEAR_USE_MX selects MXFP8 (the reference's opt-ins, in that
+// order, csrc/quantize.cu:344-357; fp32 weights go through bf16 first).
 std::tuple<at::Tensor, at::Tensor> quantize_weight(at::Tensor weight) {
   TORCH_CHECK(weight.is_cuda() && weight.dim() == 2, "weight must be a 2D CUDA tensor");
   if (at::cuda::getCurrentDeviceProperties()->major >= 10) {
-    TORCH_CHECK(std::getenv("FP8LINEAR_USE_NVFP4") == nullptr,
-                "quantize_weight: FP8LINEAR_USE_NVFP4 (NVFP4 weights) is not supported by "
-                "fp8linear_b200");
-    if (std::getenv("FP8LINEAR_USE_MX") != nullptr)
-      return quantize_mxfp8(weight.scalar_type() == at::kFloat ? weight.to(at::kBFloat16)
-                                                                : weight);
+    auto w = weight.scalar_type() == at::kFloat ? weight.to(at::kBFloat16) : weight;
+    if (std::getenv("FP8LINEAR_USE_NVFP4") != nullptr) return quantize_nvfp4(w);
+    if (std::getenv("FP8LINEAR_USE_MX") != nullptr) return quantize_mxfp8(w);
   }
   const int code = dtype_code(weight.scalar_type());
   TORCH_CHECK(code >= 0, "weight must be bf16, fp16 or fp32");
@@ -167,12 +166,10 @@ at::Tensor fp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scale,
   TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
               "x must be fp16 or bf16");
   TORCH_CHECK(x.dim() >= 1, "x must have at least one dimension");
-  // Dispatch on the weight format, as csrc/fp8_gemm.cu:206-216: e4m3 weight + uint8 scales
-  // is MXFP8; a packed uint8 weight (NVFP4) is not provided here.
+  // Dispatch on the weight format, as csrc/fp8_gemm.cu:203-216: uint8 scales with a packed
+  // uint8 weight are NVFP4, with an e4m3 weight MXFP8.
   if (w_scale.scalar_type() == at::kByte) {
-    TORCH_CHECK(wq.scalar_type() == at::kFloat8_e4m3fn,
-                "fp8_linear: NVFP4 weights (uint8 packed e2m1) are not supported by "
-                "fp8linear_b200");
+    if (wq.scalar_type() == at::kByte) return nvfp4_linear(x, wq, w_scale, bias);
     return mxfp8_linear(x, wq, w_scale, bias);
   }
   TORCH_CHECK(wq.scalar_type() == at::kFloat8_e4m3fn, "wq must be float8_e4m3fn");
@@ -202,12 +199,6 @@ at::Tensor fp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scale,
              "fp8_linear");
   }
   return out.reshape(out_shape);
-}
-
-[[noreturn]] void unsupported(const char *name) {
-  TORCH_CHECK(false, name,
-              " is not provided by fp8linear_b200: only the per-channel FP8 path "
-              "(quantize_fp8 / quantize_weight / fp8_gemm / fp8_linear) is implemented");
 }
 
 // quantize_mxfp8 (csrc/quantize.cu:239-285): same checks and outputs; the scale grid is
@@ -308,12 +299,103 @@ at::Tensor mxfp8_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scales,
   }
   return out.reshape(out_shape);
 }
-std::tuple<at::Tensor, at::Tensor> quantize_nvfp4(at::Tensor) { unsupported("quantize_nvfp4"); }
-at::Tensor nvfp4_gemm(at::Tensor, at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
-  unsupported("nvfp4_gemm");
+int64_t nv_scale_bytes(int64_t rows, int64_t K) {
+  return (rows + 127) / 128 * ((K / 16 + 3) / 4) * 512;
 }
-at::Tensor nvfp4_linear(at::Tensor, at::Tensor, at::Tensor, std::optional<at::Tensor>) {
-  unsupported("nvfp4_linear");
+
+// quantize_nvfp4 (csrc/quantize.cu:290-334): xq [M, K/2] packed e2m1, the ue4m3 scale grid
+// written whole by the kernel (the reference prefills it with 0x38).
+std::tuple<at::Tensor, at::Tensor> quantize_nvfp4(at::Tensor x) {
+  TORCH_CHECK(x.is_cuda(), "x must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
+              "x must be fp16 or bf16");
+  TORCH_CHECK(x.dim() == 2, "x must be 2D [M, K]");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto xc = aligned16(x);
+  const int64_t M = xc.size(0), K = xc.size(1);
+  TORCH_CHECK(K % 32 == 0, "K must be a multiple of 32 for NVFP4, got ", K);
+  auto xq = at::empty({M, K / 2}, xc.options().dtype(at::kByte));
+  const int64_t sf_bytes = nv_scale_bytes(M, K);
+  if (M == 0 || K == 0) {
+    return {xq, at::full({sf_bytes}, 0x38, xc.options().dtype(at::kByte))};
+  }
+  auto scales = at::empty({sf_bytes}, xc.options().dtype(at::kByte));
+  check_rc(fp8lin_quantize_nvfp4(xc.data_ptr(), dtype_code(xc.scalar_type()), M, K,
+                                 xq.data_ptr(), scales.data_ptr(), stream_of(xc)),
+           "quantize_nvfp4");
+  return {xq, scales};
+}
+
+// nvfp4_gemm (csrc/fp8_gemm.cu:352-445): the reference's checks; bf16 out (the reference
+// writes fp16).
+at::Tensor nvfp4_gemm(at::Tensor xq, at::Tensor x_scales, at::Tensor wq, at::Tensor w_scales,
+                      std::optional<at::Tensor> bias) {
+  TORCH_CHECK(xq.is_cuda() && wq.is_cuda(), "inputs must be on CUDA");
+  TORCH_CHECK(xq.scalar_type() == at::kByte && wq.scalar_type() == at::kByte,
+              "xq and wq must be packed uint8 (two e2m1 per byte)");
+  TORCH_CHECK(xq.dim() == 2 && wq.dim() == 2, "xq, wq must be 2D");
+  c10::cuda::CUDAGuard guard(xq.device());
+  auto xqc = aligned16(xq);
+  auto wqc = aligned16(wq);
+  const int64_t M = xqc.size(0), K = xqc.size(1) * 2, N = wqc.size(0);
+  TORCH_CHECK(wqc.size(1) * 2 == K, "K mismatch: xq[M,K/2], wq[N,K/2]");
+  TORCH_CHECK(K % 32 == 0, "K must be a multiple of 32 for NVFP4, got ", K);
+  TORCH_CHECK(x_scales.scalar_type() == at::kByte && w_scales.scalar_type() == at::kByte,
+              "NVFP4 scales must be uint8 (e4m3)");
+  auto xs = aligned16(x_scales);
+  auto ws = aligned16(w_scales);
+  TORCH_CHECK(xs.numel() == nv_scale_bytes(M, K),
+              "x_scales has wrong size for tiled NVFP4 layout (expected ", nv_scale_bytes(M, K),
+              ", got ", xs.numel(), ")");
+  TORCH_CHECK(ws.numel() == nv_scale_bytes(N, K),
+              "w_scales has wrong size for tiled NVFP4 layout (expected ", nv_scale_bytes(N, K),
+              ", got ", ws.numel(), ")");
+  auto out = at::empty({M, N}, xqc.options().dtype(at::kBFloat16));
+  if (M == 0 || N == 0) return out;
+  TORCH_CHECK(K > 0, "K must be positive");
+  BiasArg b = prep_bias(bias, N);
+  check_rc(fp8lin_nvfp4_gemm(xqc.data_ptr(), xs.data_ptr(), wqc.data_ptr(), ws.data_ptr(), b.ptr,
+                             b.dtype, out.data_ptr(), FP8LIN_DTYPE_BF16, M, N, K, stream_of(xqc)),
+           "nvfp4_gemm");
+  return out;
+}
+
+// nvfp4_linear (csrc/fp8_gemm.cu:447-457): x [..., K] -> [..., N] in x.dtype; wq [N, K/2].
+at::Tensor nvfp4_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scales,
+                        std::optional<at::Tensor> bias) {
+  TORCH_CHECK(x.is_cuda() && wq.is_cuda(), "inputs must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
+              "x must be fp16 or bf16");
+  TORCH_CHECK(x.dim() >= 1, "x must have at least one dimension");
+  TORCH_CHECK(wq.scalar_type() == at::kByte, "wq must be packed uint8 (two e2m1 per byte)");
+  TORCH_CHECK(wq.dim() == 2, "wq must be 2D [N, K/2]");
+  TORCH_CHECK(w_scales.scalar_type() == at::kByte, "NVFP4 scales must be uint8 (e4m3)");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(wq.size(1) * 2 == K, "K mismatch: x[..., K], wq[N, K/2]");
+  TORCH_CHECK(K % 32 == 0, "K must be a multiple of 32 for NVFP4, got ", K);
+  auto x2d = aligned16(x.reshape({-1, K}));
+  auto wqc = aligned16(wq);
+  auto ws = aligned16(w_scales);
+  const int64_t M = x2d.size(0), N = wqc.size(0);
+  TORCH_CHECK(ws.numel() == nv_scale_bytes(N, K),
+              "w_scales has wrong size for tiled NVFP4 layout (expected ", nv_scale_bytes(N, K),
+              ", got ", ws.numel(), ")");
+  auto out_shape = x.sizes().vec();
+  out_shape.back() = N;
+  auto out = at::empty({M, N}, x2d.options());
+  if (M > 0 && N > 0) {
+    TORCH_CHECK(K > 0, "K must be positive");
+    BiasArg b = prep_bias(bias, N);
+    const size_t ws_bytes = fp8lin_nvfp4_linear_workspace_size(M, K);
+    auto workspace = at::empty({static_cast<int64_t>(ws_bytes)}, x2d.options().dtype(at::kByte));
+    check_rc(fp8lin_nvfp4_linear(x2d.data_ptr(), dtype_code(x2d.scalar_type()), wqc.data_ptr(),
+                                 ws.data_ptr(), b.ptr, b.dtype, out.data_ptr(),
+                                 dtype_code(x2d.scalar_type()), M, N, K, workspace.data_ptr(),
+                                 ws_bytes, stream_of(x2d)),
+             "nvfp4_linear");
+  }
+  return out.reshape(out_shape);
 }
 
 }  // namespace

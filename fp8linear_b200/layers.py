@@ -12,8 +12,10 @@ Same public names and contracts:
 Differences from the reference: ``fp8_linear`` returns ``x.dtype`` (the reference
 returns fp16 and ``Fp8Linear.forward`` casts back); ``fp8_gemm`` returns bf16; the
 MXFP8 path (``quantize_mxfp8``, ``quantize_weight_mxfp8``, ``mxfp8_gemm``,
-``mxfp8_linear``, and ``fp8_linear`` on uint8 block scales) is implemented; the NVFP4
-entry points exist but raise ``NotImplementedError``.
+``mxfp8_linear``, and ``fp8_linear`` on uint8 block scales with an e4m3 weight) and the
+NVFP4 path (``quantize_nvfp4``, ``quantize_weight_nvfp4``, ``nvfp4_gemm``,
+``nvfp4_linear``, and ``fp8_linear`` on uint8 block scales with a packed uint8 weight) are
+implemented; ``mxfp8_gemm`` / ``nvfp4_gemm`` return bf16 and the linears ``x.dtype``.
 """
 from __future__ import annotations
 
@@ -50,6 +52,7 @@ def _fp8_gemm_fake(xq, x_scale, wq, w_scale, bias=None):
 
 
 MX_BLOCK = 32
+NV_BLOCK = 16
 
 
 def mx_scale_bytes(rows: int, K: int) -> int:
@@ -75,11 +78,27 @@ def _quantize_mxfp8_fake(x):
     return xq, scales
 
 
-def _not_provided(name: str):
-    raise NotImplementedError(
-        f"{name}: fp8linear_b200 implements the per-channel FP8 and the MXFP8 paths; "
-        "NVFP4 is not provided"
-    )
+def nv_scale_bytes(rows: int, K: int) -> int:
+    """Bytes of the NVFP4 block-scale grid: 512-byte tiles over ceil(rows/128) x
+    ceil((K/16)/4) (layers.py:50-56 of the reference)."""
+    return ((rows + 127) // 128) * ((K // NV_BLOCK + 3) // 4) * 512
+
+
+@torch.library.register_fake(add_op_namespace_prefix("quantize_nvfp4"))
+def _quantize_nvfp4_fake(x):
+    xq = x.new_empty((x.shape[0], x.shape[1] // 2), dtype=torch.uint8)
+    scales = x.new_empty((nv_scale_bytes(x.shape[0], x.shape[1]),), dtype=torch.uint8)
+    return xq, scales
+
+
+@torch.library.register_fake(add_op_namespace_prefix("nvfp4_gemm"))
+def _nvfp4_gemm_fake(xq, x_scales, wq, w_scales, bias=None):
+    return xq.new_empty((xq.shape[0], wq.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.register_fake(add_op_namespace_prefix("nvfp4_linear"))
+def _nvfp4_linear_fake(x, wq, w_scales, bias=None):
+    return x.new_empty((*x.shape[:-1], wq.shape[0]), dtype=x.dtype)
 
 
 def quantize_weight_mxfp8(weight: torch.Tensor):
@@ -102,13 +121,22 @@ def mxfp8_linear(x, wq, w_scales, bias=None):
 
 
 def quantize_weight_nvfp4(weight: torch.Tensor):
-    """Not provided (the reference's opt-in NVFP4 format); raises NotImplementedError."""
-    _not_provided("quantize_weight_nvfp4")
+    """NVFP4 block quantization of a ``[N, K]`` weight (offline; layers.py:89-98 of the
+    reference): ``(wq uint8 [N, K/2], scales uint8)``, e2m1 codes packed two per byte
+    (element 2j in the low nibble) and one ue4m3 scale per 16 weights along K in the tiled
+    block-scale layout. fp32 weights are cast to bf16 first, as the reference does."""
+    w = weight.detach()
+    if w.dtype not in (torch.float16, torch.bfloat16):
+        w = w.to(torch.bfloat16)
+    return ops.quantize_nvfp4(w.contiguous())
 
 
 def nvfp4_linear(x, wq, w_scales, bias=None):
-    """Not provided (the reference's opt-in NVFP4 format); raises NotImplementedError."""
-    _not_provided("nvfp4_linear")
+    """NVFP4 linear (layers.py:101-103 of the reference): ``wq``/``w_scales`` from
+    ``quantize_weight_nvfp4``; ``x [..., K]`` is NVFP4-quantized on the fly and multiplied
+    by the block-scaled tcgen05 e2m1 GEMM (scales inside the MMA, bias fused); returns
+    ``x.dtype``."""
+    return ops.nvfp4_linear(x, wq, w_scales, bias)
 
 
 def quantize_weight(weight: torch.Tensor):

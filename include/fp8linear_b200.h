@@ -158,6 +158,62 @@ FP8LIN_API int fp8lin_mxfp8_linear(const void *x, int x_dtype, const void *wq,
                                    void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Bytes of the NVFP4 block-scale grid for `rows` rows of K elements (K % 32 == 0):
+ * ceil(rows / 128) * ceil((K / 16) / 4) * 512 (csrc/quantize.cu:301-309, quantize_nvfp4's
+ * scales tensor size).
+ */
+FP8LIN_API size_t fp8lin_nv_scale_bytes(int64_t rows, int64_t K);
+
+/*
+ * NVFP4 block quantization: e2m1 codes packed two per byte, one ue4m3 scale per 16
+ * elements along K. Replaces quantize_nvfp4 (csrc/quantize.cu:290-334; kernel
+ * csrc/quantize.cu:157-194); applies to activations and, offline, to weights
+ * (quantize_weight_nvfp4).
+ *   x      [M, K] row-major, x_dtype BF16 or F16, K % 32 == 0, 16-byte aligned
+ *   xq     [M, K/2] bytes, 4-byte aligned: element 2j in the low nibble of byte j
+ *   scales fp8lin_nv_scale_bytes(M, K) bytes, 4-byte aligned, in the tiled layout of
+ *          fp8lin_quantize_mxfp8 with ncb = ceil((K/16)/4); padding entries are written
+ *          with 0x38 (e4m3 1.0), so the buffer needs no prefill.
+ * Per block: s = e4m3_satfinite(min(amax * fl(1/6), 448)); codes = e2m1 of
+ * clamp(x * (1 / s), -6, 6) by the round-to-nearest thresholds (ties up), 1/s = 0 when
+ * s = 0. Codes and scales are bit-identical to the reference kernel. M == 0 is a no-op.
+ */
+FP8LIN_API int fp8lin_quantize_nvfp4(const void *x, int x_dtype, int64_t M, int64_t K,
+                                     void *xq, void *scales, void *stream);
+
+/*
+ * NVFP4 GEMM with block scales applied inside the tensor-core MMA and the bias fused.
+ * Replaces nvfp4_gemm (csrc/fp8_gemm.cu:352-445: cuBLASLt VEC16_UE4M3 block-scaled e2m1
+ * matmul, bias epilogue, fp16 out), here one tcgen05 kind::mxf4nvf4.block_scale kernel:
+ *   out[m,n] = sum_k e2m1(xq[m,k]) xs[m,k/16] * e2m1(wq[n,k]) ws[n,k/16] + bias[n]
+ *   xq [M, K/2], wq [N, K/2] packed e2m1 (fp8lin_quantize_nvfp4), 16-byte aligned;
+ *   K (elements) % 32 == 0
+ *   x_scales / w_scales: the tiled ue4m3 grids for M / N rows (fp8lin_nv_scale_bytes
+ *   bytes), 16-byte aligned
+ *   bias [N] BF16/F16/F32 or NULL; out [M,N] BF16 or F16 (the reference writes fp16)
+ * M == 0 or N == 0 is a no-op.
+ */
+FP8LIN_API int fp8lin_nvfp4_gemm(const void *xq, const void *x_scales, const void *wq,
+                                 const void *w_scales, const void *bias, int bias_dtype,
+                                 void *out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                 void *stream);
+
+/* Workspace fp8lin_nvfp4_linear needs: the packed codes (M*K/2) and the scale grid, each
+ * rounded up to 256 bytes. */
+FP8LIN_API size_t fp8lin_nvfp4_linear_workspace_size(int64_t M, int64_t K);
+
+/*
+ * Fused NVFP4 linear: fp8lin_quantize_nvfp4 of x into the workspace, then the block-scaled
+ * GEMM launched as its programmatic dependent. Replaces nvfp4_linear
+ * (csrc/fp8_gemm.cu:447-457) and the NVFP4 branch of fp8_linear (csrc/fp8_gemm.cu:206-209).
+ * wq / w_scales from fp8lin_quantize_nvfp4 of the weight (quantize_weight_nvfp4).
+ */
+FP8LIN_API int fp8lin_nvfp4_linear(const void *x, int x_dtype, const void *wq,
+                                   const void *w_scales, const void *bias, int bias_dtype,
+                                   void *out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                   void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Device workspace fp8lin_fp8_linear needs for M tokens of width K: the e4m3 codes
  * and the per-token scales of x (aligned sub-buffers).
  */

@@ -99,16 +99,3 @@ def test_quantize_and_fp8linear_module():
     assert out.dtype == torch.bfloat16 and out.shape == (4, 33, 128)
     rel = float((out.float() - ref_out).norm() / ref_out.norm())
     assert rel < 0.1
-
-
-def test_linear_rejects_nvfp4_weights():
-    """uint8 scales with an e4m3 weight are MXFP8 (tests/test_mx_gemm_gpu.py); with a packed
-    uint8 weight they are NVFP4, which is not provided and raises."""
-    import fp8linear_b200 as f
-
-    x = torch.randn(4, 64, device="cuda", dtype=torch.bfloat16)
-    wq4 = torch.zeros(16, 32, dtype=torch.uint8, device="cuda")
-    with pytest.raises(RuntimeError, match="NVFP4"):
-        f.fp8_linear(x, wq4, torch.zeros(512, dtype=torch.uint8, device="cuda"), None)
-    with pytest.raises(NotImplementedError):
-        f.quantize_weight_nvfp4(x)

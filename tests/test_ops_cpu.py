@@ -70,5 +70,27 @@ def test_block_scaled_entry_points_raise():
         f.mxfp8_linear(torch.zeros(2, 32, dtype=torch.bfloat16),
                        torch.zeros(4, 32, dtype=torch.float8_e4m3fn),
                        torch.zeros(512, dtype=torch.uint8))
-    with pytest.raises(NotImplementedError):
-        f.nvfp4_linear(None, None, None)
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        f.quantize_weight_nvfp4(torch.zeros(4, 32))
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        f.nvfp4_linear(torch.zeros(2, 32, dtype=torch.bfloat16),
+                       torch.zeros(4, 16, dtype=torch.uint8),
+                       torch.zeros(512, dtype=torch.uint8))
+
+
+def test_block_scaled_fake_impls():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        x = torch.empty(300, 3072, dtype=torch.bfloat16)
+        xq, xs = f.ops.quantize_nvfp4(x)
+        assert xq.shape == (300, 1536) and xq.dtype == torch.uint8
+        assert xs.shape == (3 * 48 * 512,) and xs.dtype == torch.uint8
+        wq = torch.empty(9216, 1536, dtype=torch.uint8)
+        ws = torch.empty(72 * 48 * 512, dtype=torch.uint8)
+        assert f.ops.nvfp4_gemm(xq, xs, wq, ws, None).dtype == torch.bfloat16
+        o = f.ops.nvfp4_linear(x.half().view(3, 100, 3072), wq, ws, None)
+        assert o.shape == (3, 100, 9216) and o.dtype == torch.float16
+        mq, ms = f.ops.quantize_mxfp8(x)
+        assert mq.shape == (300, 3072) and ms.shape == (3 * 24 * 512,)
+    assert f.layers.nv_scale_bytes(300, 3072) == 3 * 48 * 512
