@@ -667,11 +667,16 @@ __global__ void __launch_bounds__(32 * kMxWarps) quant_mx_kernel(
 // Lane l holds 8 consecutive elements of vector i (16 bytes): a block is 2 lanes, a
 // 4-block group of scales (one 32-bit word of the layout) is 8 lanes. Padding scales are
 // 0x38 (e4m3 1.0), written by the kernel.
+// The magnitude code of |v| <= 6 by the thresholds above. Each threshold has at most two
+// mantissa bits, so a >= t exactly when (exponent, top two mantissa bits) of a are >= those of
+// t: the code is a function of bits 21-30 of a. From 0.25 (exponent 125) upwards those index
+// a table of 19 3-bit codes; below 0.25 the code is 0. (Checked against the threshold form
+// for every float in [0, 6].)
+constexpr uint64_t kE2m1Lut = 0x01fed6c8da489249ull;  // codes 1,1,1,1,1,1,2,2,2,3,3,4,4,5,5,6,6,7,7
 __device__ __forceinline__ uint32_t e2m1_code(float v) {
   const uint32_t sgn = v < 0.0f ? 8u : 0u;
-  const float a = fabsf(v);
-  const uint32_t c = a < 0.25f ? 0u : a < 0.75f ? 1u : a < 1.25f ? 2u : a < 1.75f ? 3u
-                   : a < 2.5f  ? 4u : a < 3.5f  ? 5u : a < 5.0f  ? 6u : 7u;
+  const int idx = static_cast<int>((__float_as_uint(v) & 0x7FFFFFFFu) >> 21) - (125 << 2);
+  const uint32_t c = idx < 0 ? 0u : static_cast<uint32_t>(kE2m1Lut >> (3 * idx)) & 7u;
   return sgn | c;
 }
 
