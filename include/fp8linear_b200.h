@@ -101,7 +101,9 @@ FP8LIN_API int fp8lin_quantize_mxfp8(const void *x, int x_dtype, int64_t M, int6
  *   w       [N, K] row-major, w_dtype BF16, F16 or F32
  *   wq      [N, K] e4m3fn codes; w_scale [N] fp32. NaN propagates as in ATen.
  * The reference's opt-in MXFP8/NVFP4 diversions (FP8LINEAR_USE_MX /
- * FP8LINEAR_USE_NVFP4, csrc/quantize.cu:344-357) are not part of this library.
+ * FP8LINEAR_USE_NVFP4, csrc/quantize.cu:344-357) are applied by the torch op
+ * quantize_weight, which calls fp8lin_quantize_mxfp8 / fp8lin_quantize_nvfp4 instead;
+ * this entry point is the per-channel quantizer only.
  */
 FP8LIN_API int fp8lin_quantize_weight(const void *w, int w_dtype, int64_t N, int64_t K,
                                       void *wq, float *w_scale, void *stream);
