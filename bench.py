@@ -196,13 +196,15 @@ def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True, fmt
     """``n_sets`` independent (x, wq, ws, bias[, xq, xs]) sets of workload ``wl`` on
     the current device (weights quantized once, as offline). Set i's weight depends
     only on i, so ranks hold the same weights; activations use ``x_seed0``. ``fmt``
-    "fp8": per-token / per-channel scales; "mx": MXFP8 block scales; "nv": NVFP4."""
+    "fp8": per-token / per-channel scales; "mx": MXFP8 block scales; "nv": NVFP4;
+    "modulated": per-channel weights plus the AdaLN shift / scale [2, K] of a 2-image batch."""
     import fp8linear_b200 as f
     from fp8linear_b200.workloads import make_weight, make_x
 
     qw = {"fp8": f.quantize_weight, "mx": f.quantize_weight_mxfp8,
-          "nv": f.quantize_weight_nvfp4}[fmt]
-    qx = {"fp8": f.quantize_fp8, "mx": f.quantize_mxfp8, "nv": f.quantize_nvfp4}[fmt]
+          "nv": f.quantize_weight_nvfp4, "modulated": f.quantize_weight}[fmt]
+    qx = {"fp8": f.quantize_fp8, "mx": f.quantize_mxfp8, "nv": f.quantize_nvfp4,
+          "modulated": f.quantize_fp8}[fmt]
     sets = []
     for i in range(n_sets):
         x = make_x(wl, seed=x_seed0 + 7919 * i, gen_device="cuda")
@@ -210,10 +212,28 @@ def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True, fmt
         wq, ws = qw(w)
         del w
         s = {"x": x, "wq": wq, "ws": ws, "b": b}
+        if fmt == "modulated":
+            s["shift"], s["scale"] = modulation(wl, 7919 * i + 17)
         if quantize_x:
             s["xq"], s["xs"] = qx(x)
         sets.append(s)
     return sets
+
+
+def modulation(wl, seed: int):
+    """AdaLN shift and scale [2, K] (a 2-image batch; M divisible by 2), bf16."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    shift = (torch.randn(2, wl.K, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    scale = (torch.randn(2, wl.K, device="cuda", generator=g) * 0.2).to(torch.bfloat16)
+    return shift, scale
+
+
+def unfused_modulation(x, shift, scale, eps=1e-6):
+    """The chain a FLUX block runs before its linear without the fusion: torch LayerNorm
+    (no affine) and the bf16 modulation ops."""
+    K = x.shape[-1]
+    b = torch.arange(x.shape[0], device=x.device) // (x.shape[0] // shift.shape[0])
+    return torch.nn.functional.layer_norm(x, (K,), eps=eps) * (1 + scale)[b] + shift[b]
 
 
 def per_set_bytes(wl) -> int:
@@ -488,18 +508,31 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
         del g
         return ms
 
-    lin_op, gemm_op, quant_op = {
-        "fp8": (f.fp8_linear, f.fp8_gemm, f.quantize_fp8),
-        "mx": (f.mxfp8_linear, f.mxfp8_gemm, f.quantize_mxfp8),
-        "nv": (f.nvfp4_linear, f.nvfp4_gemm, f.quantize_nvfp4)}[fmt]
-    fused = timed(lambda st: lin_op(st["x"], st["wq"], st["ws"], st["b"]))
-    gemm = timed(lambda st: gemm_op(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
-    quant = timed(lambda st: quant_op(st["x"]))
+    extra = {}
+    if fmt == "modulated":
+        fused = timed(lambda st: f.fp8_linear_modulated(st["x"], st["shift"], st["scale"], st["wq"],
+                                                        st["ws"], st["b"]))
+        gemm = timed(lambda st: f.fp8_gemm(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
+        quant = timed(lambda st: f.layernorm_modulate_quantize_fp8(st["x"], st["shift"],
+                                                                   st["scale"]))
+        unf = timed(lambda st: f.fp8_linear(unfused_modulation(st["x"], st["shift"], st["scale"]),
+                                            st["wq"], st["ws"], st["b"]))
+        unq = timed(lambda st: f.quantize_fp8(unfused_modulation(st["x"], st["shift"],
+                                                                 st["scale"])))
+        extra = {"unfused_us": round(unf * 1e3, 2), "unfused_quant_us": round(unq * 1e3, 2)}
+    else:
+        lin_op, gemm_op, quant_op = {
+            "fp8": (f.fp8_linear, f.fp8_gemm, f.quantize_fp8),
+            "mx": (f.mxfp8_linear, f.mxfp8_gemm, f.quantize_mxfp8),
+            "nv": (f.nvfp4_linear, f.nvfp4_gemm, f.quantize_nvfp4)}[fmt]
+        fused = timed(lambda st: lin_op(st["x"], st["wq"], st["ws"], st["b"]))
+        gemm = timed(lambda st: gemm_op(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
+        quant = timed(lambda st: quant_op(st["x"]))
     # quantizer bytes: read 2MK, write the codes (MK, NV MK/2) and the scales (4M fp32,
     # MK/32 e8m0, MK/16 ue4m3)
     mk = wl.M * wl.K
     qbytes = {"fp8": 3 * mk + 4 * wl.M, "mx": 3 * mk + mk // 32,
-              "nv": 2 * mk + mk // 2 + mk // 16}[fmt]
+              "nv": 2 * mk + mk // 2 + mk // 16, "modulated": 3 * mk + 4 * wl.M}[fmt]
     pk = peaks()
     # bandwidth-aware roofline for the GEMM: min(tensor peak, AI x HBM); the e4m3 forms run
     # at 2x and e2m1 at 4x the measured bf16 rate (the nominal dense ratios), and the NVFP4
@@ -519,7 +552,7 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
             "gemm_roofline_tflops": round(roof, 1), "gemm_frac": round(g_tf / roof, 4),
             "quant_us": round(quant * 1e3, 2),
             "quant_gbs": round(qbytes / (quant * 1e-3) / 1e9, 1),
-            "quant_frac": round(qbytes / (quant * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+            "quant_frac": round(qbytes / (quant * 1e-3) / 1e9 / pk["hbm_gbs"], 4), **extra}
 
 
 def reference_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> dict:
@@ -722,15 +755,23 @@ def reference_gpu_timing(wl, args, fmt: str = "fp8"):
     for i in range(n_sets):
         x = make_x(wl, seed=7919 * i, gen_device="cuda")
         w, b = make_weight(wl, seed=7919 * i, gen_device="cuda")
-        qw = {"fp8": ref.quantize_weight, "mx": ref.quantize_mxfp8, "nv": ref.quantize_nvfp4}[fmt]
+        qw = {"fp8": ref.quantize_weight, "mx": ref.quantize_mxfp8, "nv": ref.quantize_nvfp4,
+              "modulated": ref.quantize_weight}[fmt]
         wq, ws = qw(w)
-        sets.append({"x": x, "wq": wq, "ws": ws, "b": b})
+        st = {"x": x, "wq": wq, "ws": ws, "b": b}
+        if fmt == "modulated":
+            st["shift"], st["scale"] = modulation(wl, 7919 * i + 17)
+        sets.append(st)
         del w
     stream = torch.cuda.current_stream(dev)
-    lin = {"fp8": ref.fp8_linear, "mx": ref.mxfp8_linear, "nv": ref.nvfp4_linear}[fmt]
+    lin = {"fp8": ref.fp8_linear, "mx": ref.mxfp8_linear, "nv": ref.nvfp4_linear,
+           "modulated": ref.fp8_linear}[fmt]
 
     def call(st):
-        return lin(st["x"], st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
+        x = st["x"]
+        if fmt == "modulated":  # the FLUX block's LayerNorm + modulation before the linear
+            x = unfused_modulation(x, st["shift"], st["scale"])
+        return lin(x, st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
 
     try:
         call(sets[0])
@@ -777,9 +818,10 @@ def main():
                          "channels with an NCCL all-gather")
     ap.add_argument("--fused", action="store_true",
                     help="with --mode nshard: fuse the all-gather into the GEMM epilogue")
-    ap.add_argument("--format", choices=["fp8", "mx", "nv"], default="fp8",
+    ap.add_argument("--format", choices=["fp8", "mx", "nv", "modulated"], default="fp8",
                     help="with --sweep: per-channel FP8 ops (default), the MXFP8 or the "
-                         "NVFP4 ops")
+                         "NVFP4 ops, or the LayerNorm + modulation fused into the quantizer "
+                         "against the unfused FLUX chain")
     ap.add_argument("--sweep", default="",
                     help="'all' or comma-separated workloads: one JSON line of per-kernel "
                          "device times per workload (not the driver's line)")

@@ -9,6 +9,8 @@ from ._ops import ops
 from .layers import (
     Fp8Linear,
     fp8_linear,
+    fp8_linear_modulated,
+    layernorm_modulate_quantize_fp8,
     mxfp8_linear,
     nvfp4_linear,
     quantize_,
@@ -41,4 +43,6 @@ __all__ = [
     "quantize_weight_nvfp4",
     "quantize_nvfp4",
     "nvfp4_gemm",
+    "layernorm_modulate_quantize_fp8",
+    "fp8_linear_modulated",
 ]

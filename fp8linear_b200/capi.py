@@ -19,7 +19,7 @@ DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 DTYPE_NONE = -1
 
 # name -> (restype, argtypes); mirrors the declarations in include/fp8linear_b200.h
-_P, _I, _I64, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+_P, _I, _I64, _SZ, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float
 SIGNATURES = {
     "fp8lin_abi_version": (_I, []),
     "fp8lin_build_info": (ctypes.c_char_p, []),
@@ -31,6 +31,9 @@ SIGNATURES = {
     "fp8lin_mxfp8_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
     "fp8lin_mxfp8_linear_workspace_size": (_SZ, [_I64, _I64]),
     "fp8lin_mxfp8_linear": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
+    "fp8lin_layernorm_modulate_quantize_fp8": (_I, [_P, _I, _I64, _I64, _I64, _P, _P, _F, _P, _P, _P]),
+    "fp8lin_fp8_linear_modulated": (_I, [_P, _I, _I64, _I64, _I64, _P, _P, _F, _P, _P, _P, _I, _P,
+                                        _I, _I64, _P, _SZ, _P]),
     "fp8lin_nv_scale_bytes": (_SZ, [_I64, _I64]),
     "fp8lin_quantize_nvfp4": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
     "fp8lin_nvfp4_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
@@ -173,6 +176,34 @@ class CApi:
                                           DTYPE[out.dtype], M, N, K, workspace.data_ptr(),
                                           workspace.numel(), self._stream(x))
         self._check(rc, "fp8lin_nvfp4_linear")
+        return out
+
+    def layernorm_modulate_quantize_fp8(self, x, shift, scale, eps=1e-6, xq=None, x_scale=None):
+        K = x.shape[-1]
+        M = x.numel() // K
+        xq = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device) if xq is None else xq
+        x_scale = torch.empty((M,), dtype=torch.float32, device=x.device) if x_scale is None else x_scale
+        rc = self.lib.fp8lin_layernorm_modulate_quantize_fp8(
+            x.data_ptr(), DTYPE[x.dtype], M, K, shift.shape[0], shift.data_ptr(),
+            scale.data_ptr(), float(eps), xq.data_ptr(), x_scale.data_ptr(), self._stream(x))
+        self._check(rc, "fp8lin_layernorm_modulate_quantize_fp8")
+        return xq, x_scale
+
+    def fp8_linear_modulated(self, x, shift, scale, wq, w_scale, bias=None, eps=1e-6, out=None,
+                             workspace=None):
+        K = x.shape[-1]
+        M = x.numel() // K
+        N = wq.shape[0]
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device) if out is None else out
+        need = int(self.lib.fp8lin_linear_workspace_size(M, K))
+        if workspace is None:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+        rc = self.lib.fp8lin_fp8_linear_modulated(
+            x.data_ptr(), DTYPE[x.dtype], M, K, shift.shape[0], shift.data_ptr(),
+            scale.data_ptr(), float(eps), wq.data_ptr(), w_scale.data_ptr(), self._bias_ptr(bias),
+            self._bias_dtype(bias), out.data_ptr(), DTYPE[out.dtype], N, workspace.data_ptr(),
+            workspace.numel(), self._stream(x))
+        self._check(rc, "fp8lin_fp8_linear_modulated")
         return out
 
     def quantize_weight(self, w: torch.Tensor):

@@ -380,6 +380,80 @@ int fp8lin_nvfp4_linear(const void *x, int x_dtype, const void *wq, const void *
   return launch_gemm(a, s, true);
 }
 
+static int check_modulation(const void *x, int x_dtype, int64_t M, int64_t K, int64_t batches,
+                     const void *shift, const void *scale, float eps, const char *op) {
+  const std::string o(op);
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": x must be fp16 or bf16");
+  if (M < 0 || K < 0) return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": negative size");
+  if (K % 8 != 0 || K == 0 || K > kLnMaxK)
+    return fail(FP8LIN_ERR_UNSUPPORTED,
+                o + ": K must be a positive multiple of 8 up to 8192, got " + std::to_string(K));
+  if (batches <= 0 || (M > 0 && M % batches != 0))
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT,
+                o + ": batches must be positive and divide M (rows " + std::to_string(M) +
+                    ", batches " + std::to_string(batches) + ")");
+  if (!(eps >= 0.0f)) return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": eps must be >= 0");
+  if (M == 0) return FP8LIN_OK;
+  if (!x || !shift || !scale) return fail(FP8LIN_ERR_INVALID_ARGUMENT, o + ": null pointer");
+  if (!aligned(x, 16) || !aligned(shift, 16) || !aligned(scale, 16))
+    return fail(FP8LIN_ERR_UNSUPPORTED, o + ": x, shift and scale must be 16-byte aligned");
+  return FP8LIN_OK;
+}
+
+int fp8lin_layernorm_modulate_quantize_fp8(const void *x, int x_dtype, int64_t M, int64_t K,
+                                           int64_t batches, const void *shift,
+                                           const void *scale, float eps, void *xq,
+                                           float *x_scale, void *stream) {
+  clear_error();
+  int rc = check_modulation(x, x_dtype, M, K, batches, shift, scale, eps,
+                            "layernorm_modulate_quantize_fp8");
+  if (rc != FP8LIN_OK || M == 0) return rc;
+  if (!xq || !x_scale)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "layernorm_modulate_quantize_fp8: null output");
+  if (!aligned(xq, 8) || !aligned(x_scale, 4))
+    return fail(FP8LIN_ERR_UNSUPPORTED,
+                "layernorm_modulate_quantize_fp8: xq must be 8-byte, x_scale 4-byte aligned");
+  cudaError_t e = launch_ln_modulate_quantize(x, x_dtype, M, K, batches, shift, scale, eps,
+                                              static_cast<uint8_t *>(xq), x_scale,
+                                              static_cast<cudaStream_t>(stream), false);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("layernorm_modulate_quantize_fp8: launch: ") +
+                                     cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
+int fp8lin_fp8_linear_modulated(const void *x, int x_dtype, int64_t M, int64_t K,
+                                int64_t batches, const void *shift, const void *scale, float eps,
+                                const void *wq, const float *w_scale, const void *bias,
+                                int bias_dtype, void *out, int out_dtype, int64_t N,
+                                void *workspace, size_t workspace_bytes, void *stream) {
+  clear_error();
+  int rc = check_modulation(x, x_dtype, M, K, batches, shift, scale, eps, "fp8_linear_modulated");
+  if (rc != FP8LIN_OK) return rc;
+  rc = check_gemm_args(reinterpret_cast<const void *>(16), w_scale, wq, w_scale, bias, bias_dtype,
+                       out, out_dtype, M, N, K, "fp8_linear_modulated");
+  if (rc != FP8LIN_OK || M == 0 || N == 0) return rc;
+  const size_t need = fp8lin_linear_workspace_size(M, K);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, kWsAlign))
+    return fail(FP8LIN_ERR_WORKSPACE, "fp8_linear_modulated: workspace of " +
+                                          std::to_string(need) +
+                                          " bytes (256-byte aligned) required, got " +
+                                          std::to_string(workspace_bytes));
+  uint8_t *xq = static_cast<uint8_t *>(workspace);
+  float *xs = reinterpret_cast<float *>(
+      xq + round_up(static_cast<size_t>(M) * static_cast<size_t>(K), kWsAlign));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_ln_modulate_quantize(x, x_dtype, M, K, batches, shift, scale, eps, xq, xs,
+                                              s, true);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("fp8_linear_modulated: quantize launch: ") +
+                                     cudaGetErrorString(e));
+  GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
+             bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  return launch_gemm(a, s, true);
+}
+
 int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, const float *w_scale,
                                 const void *bias, int bias_dtype, void *const *outs, int n_outs,
                                 int out_dtype, int64_t M, int64_t N, int64_t K, int64_t ldo,

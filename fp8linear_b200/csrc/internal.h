@@ -49,6 +49,14 @@ cudaError_t launch_quantize_nv(const void *x, int dtype, int64_t M, int64_t K, u
 inline int64_t nv_scale_bytes(int64_t rows, int64_t K) {
   return (rows + 127) / 128 * ((K / 16 + 3) / 4) * 512;
 }
+// LayerNorm (no affine) + modulation y = LN(x) * (1 + scale[b]) + shift[b], then the
+// per-token e4m3 quantizer on y; rows m of batch b = m / (M / batches); shift and scale
+// [batches, K] of x's dtype, 16-byte aligned rows. K % 8 == 0, K <= kLnMaxK.
+constexpr int64_t kLnMaxK = 8192;
+cudaError_t launch_ln_modulate_quantize(const void *x, int dtype, int64_t M, int64_t K,
+                                        int64_t batches, const void *shift, const void *scale,
+                                        float eps, uint8_t *xq, float *x_scale,
+                                        cudaStream_t stream, bool trigger_dependents);
 // Reads (and optionally clears) the quantizer watchdog bits (8) of the current device.
 cudaError_t read_quant_status(unsigned int *bits, bool clear);
 // Per-channel weight quantization (ATen semantics of the reference's quantize_weight).

@@ -775,6 +775,161 @@ cudaError_t launch_mx_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, ui
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- LayerNorm + modulation
+//
+// The quantizer fused into the op that precedes the linear in a FLUX / DiT block
+// (AdaLayerNormZero: y = LayerNorm(x) * (1 + scale[b]) + shift[b], LayerNorm without
+// affine parameters), so that the modulated activations never go to HBM in bf16: the
+// kernel reads x and writes the e4m3 codes and per-token scales the GEMM consumes.
+// y is rounded to x's type after each step exactly as the unfused bf16 torch ops round it
+//   ln = T((x - mean) * rstd); m1 = T(1 + scale); t = T(ln * m1); y = T(t + shift)
+// and is then quantized with the reference's per-token rule (quant8_clamp, the literal
+// clamp arithmetic of csrc/quantize.cu:52-72). mean and the variance are fp32 sums in a
+// fixed order -- lane l adds the elements of its 8-element chunks l, l + 32, ... in
+// sequence, then a butterfly over xor offsets 16, 8, 4, 2, 1 -- and
+// rstd = 1 / sqrt(var + eps) with IEEE square root and divides, so the result is
+// reproducible exactly on the CPU.
+// One warp per row holding the row in registers (K <= 8192, K % 8 == 0); 8 rows per CTA.
+constexpr int kLnThreads = 256;
+
+template <typename T>
+struct Rnd;
+template <>
+struct Rnd<__nv_bfloat16> {
+  __device__ __forceinline__ static uint32_t bits(float v) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+  __device__ __forceinline__ static float val(uint32_t b) { return __uint_as_float(b << 16); }
+};
+template <>
+struct Rnd<__half> {
+  __device__ __forceinline__ static uint32_t bits(float v) {
+    return __half_as_ushort(__float2half_rn(v));
+  }
+  __device__ __forceinline__ static float val(uint32_t b) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+  }
+};
+
+__device__ __forceinline__ float warp_sum_xor(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T, int CPL>
+__global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
+    const T *__restrict__ x, const T *__restrict__ shift, const T *__restrict__ scale, int64_t M,
+    int K, int64_t rows_per_batch, float eps, uint8_t *__restrict__ xq, float *__restrict__ xs,
+    int trigger) {
+  if (trigger) ptx::grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kLnThreads / 32) + (threadIdx.x >> 5);
+  if (row >= M) return;  // warp-uniform
+  const int nch = K >> 3;
+  const T *xr = x + row * static_cast<int64_t>(K);
+  uint4 v[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < nch ? ld_stream_v4(xr + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  const float kf = static_cast<float>(K);
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    if (lane + 32 * i < nch) {
+      float f[8];
+      In<T>::unpack8(v[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum = __fadd_rn(sum, f[e]);
+    }
+  }
+  const float mean = __fdiv_rn(warp_sum_xor(sum), kf);
+  float sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    if (lane + 32 * i < nch) {
+      float f[8];
+      In<T>::unpack8(v[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = __fsub_rn(f[e], mean);
+        sq = __fadd_rn(sq, __fmul_rn(d, d));
+      }
+    }
+  }
+  const float var = __fdiv_rn(warp_sum_xor(sq), kf);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  const int64_t boff = (row / rows_per_batch) * static_cast<int64_t>(K);
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nch) {
+      float f[8], fs[8], fh[8];
+      In<T>::unpack8(v[i], f);
+      In<T>::unpack8(__ldg(reinterpret_cast<const uint4 *>(scale + boff + 8 * c)), fs);
+      In<T>::unpack8(__ldg(reinterpret_cast<const uint4 *>(shift + boff + 8 * c)), fh);
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        uint32_t b2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float ln = Rnd<T>::val(Rnd<T>::bits(__fmul_rn(__fsub_rn(f[e + h], mean), rstd)));
+          const float m1 = Rnd<T>::val(Rnd<T>::bits(__fadd_rn(1.0f, fs[e + h])));
+          const float t = Rnd<T>::val(Rnd<T>::bits(__fmul_rn(ln, m1)));
+          b2[h] = Rnd<T>::bits(__fadd_rn(t, fh[e + h]));
+          amax = fmaxf(amax, fabsf(Rnd<T>::val(b2[h])));
+        }
+        w[e >> 1] = b2[0] | (b2[1] << 16);
+      }
+      v[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  amax = warp_max(amax);
+  const float sc = fmaxf(__fdiv_rn(amax, kE4M3Max), kScaleFloor);
+  const float inv = __fdiv_rn(1.0f, sc);
+  if (lane == 0) xs[row] = sc;
+  uint8_t *qr = xq + row * static_cast<int64_t>(K);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nch) *reinterpret_cast<uint2 *>(qr + 8 * c) = quant8_clamp<T>(v[i], inv);
+  }
+}
+
+template <typename T, int CPL>
+cudaError_t launch_ln_cpl(const void *x, const void *shift, const void *scale, int64_t M, int K,
+                          int64_t rows_per_batch, float eps, uint8_t *xq, float *xs,
+                          cudaStream_t stream, bool trigger) {
+  const int64_t blocks = (M + kLnThreads / 32 - 1) / (kLnThreads / 32);
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  ln_mod_quant_kernel<T, CPL><<<static_cast<unsigned>(blocks), kLnThreads, 0, stream>>>(
+      reinterpret_cast<const T *>(x), reinterpret_cast<const T *>(shift),
+      reinterpret_cast<const T *>(scale), M, K, rows_per_batch, eps, xq, xs, trigger ? 1 : 0);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_ln_typed(const void *x, const void *shift, const void *scale, int64_t M,
+                            int K, int64_t rows_per_batch, float eps, uint8_t *xq, float *xs,
+                            cudaStream_t stream, bool trigger) {
+  const int per_lane = (K / 8 + 31) / 32;  // 16-byte chunks per lane
+  if (per_lane <= 4)
+    return launch_ln_cpl<T, 4>(x, shift, scale, M, K, rows_per_batch, eps, xq, xs, stream, trigger);
+  if (per_lane <= 8)
+    return launch_ln_cpl<T, 8>(x, shift, scale, M, K, rows_per_batch, eps, xq, xs, stream, trigger);
+  if (per_lane <= 12)
+    return launch_ln_cpl<T, 12>(x, shift, scale, M, K, rows_per_batch, eps, xq, xs, stream, trigger);
+  if (per_lane <= 16)
+    return launch_ln_cpl<T, 16>(x, shift, scale, M, K, rows_per_batch, eps, xq, xs, stream, trigger);
+  if (per_lane <= 24)
+    return launch_ln_cpl<T, 24>(x, shift, scale, M, K, rows_per_batch, eps, xq, xs, stream, trigger);
+  return launch_ln_cpl<T, 32>(x, shift, scale, M, K, rows_per_batch, eps, xq, xs, stream, trigger);
+}
+
 }  // namespace
 
 cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
@@ -799,6 +954,21 @@ cudaError_t launch_quantize_nv(const void *x, int dtype, int64_t M, int64_t K, u
   if (dtype == kBF16)
     return launch_nv_typed<__nv_bfloat16>(x, M, K, xq, scales, stream, trigger_dependents);
   return launch_nv_typed<__half>(x, M, K, xq, scales, stream, trigger_dependents);
+}
+
+cudaError_t launch_ln_modulate_quantize(const void *x, int dtype, int64_t M, int64_t K,
+                                        int64_t batches, const void *shift, const void *scale,
+                                        float eps, uint8_t *xq, float *x_scale,
+                                        cudaStream_t stream, bool trigger_dependents) {
+  if (M == 0) return cudaSuccess;
+  if (K <= 0 || K > kLnMaxK || K % 8 != 0 || batches <= 0 || M % batches != 0)
+    return cudaErrorInvalidValue;
+  const int64_t rpb = M / batches;
+  if (dtype == kBF16)
+    return launch_ln_typed<__nv_bfloat16>(x, shift, scale, M, static_cast<int>(K), rpb, eps, xq,
+                                          x_scale, stream, trigger_dependents);
+  return launch_ln_typed<__half>(x, shift, scale, M, static_cast<int>(K), rpb, eps, xq, x_scale,
+                                 stream, trigger_dependents);
 }
 
 cudaError_t read_quant_status(unsigned int *bits, bool clear) {

@@ -398,6 +398,84 @@ at::Tensor nvfp4_linear(at::Tensor x, at::Tensor wq, at::Tensor w_scales,
   return out.reshape(out_shape);
 }
 
+// Modulated input (no reference op; it fuses the chain that feeds Fp8Linear in a FLUX
+// block): x [B, T, K] or [M, K], shift and scale [B, K] of x's dtype (B divides M).
+struct ModArgs {
+  at::Tensor x2d, shift, scale;
+  int64_t M = 0, K = 0, B = 0;
+};
+
+ModArgs prep_modulation(const at::Tensor &x, const at::Tensor &shift, const at::Tensor &scale,
+                        const char *op) {
+  TORCH_CHECK(x.is_cuda() && shift.is_cuda() && scale.is_cuda(), op, ": inputs must be on CUDA");
+  TORCH_CHECK(x.scalar_type() == at::kHalf || x.scalar_type() == at::kBFloat16,
+              op, ": x must be fp16 or bf16");
+  TORCH_CHECK(shift.scalar_type() == x.scalar_type() && scale.scalar_type() == x.scalar_type(),
+              op, ": shift and scale must have x's dtype");
+  TORCH_CHECK(x.dim() == 2 || x.dim() == 3, op, ": x must be [M, K] or [B, T, K]");
+  TORCH_CHECK(shift.dim() == 2 && scale.dim() == 2 && shift.sizes() == scale.sizes(),
+              op, ": shift and scale must be [B, K]");
+  ModArgs a;
+  a.K = x.size(-1);
+  a.B = shift.size(0);
+  TORCH_CHECK(shift.size(1) == a.K, op, ": shift/scale width must equal x's last dim");
+  if (x.dim() == 3) TORCH_CHECK(x.size(0) == a.B, op, ": x [B, T, K] needs shift/scale [B, K]");
+  a.x2d = aligned16(x.reshape({-1, a.K}));
+  a.M = a.x2d.size(0);
+  TORCH_CHECK(a.B > 0 && a.M % a.B == 0, op, ": the batch count must divide the rows");
+  TORCH_CHECK(a.K % 8 == 0 && a.K > 0 && a.K <= 8192, op,
+              ": K must be a positive multiple of 8 up to 8192, got ", a.K);
+  a.shift = aligned16(shift);
+  a.scale = aligned16(scale);
+  return a;
+}
+
+std::tuple<at::Tensor, at::Tensor> layernorm_modulate_quantize_fp8(at::Tensor x, at::Tensor shift,
+                                                                   at::Tensor scale, double eps) {
+  c10::cuda::CUDAGuard guard(x.device());
+  ModArgs a = prep_modulation(x, shift, scale, "layernorm_modulate_quantize_fp8");
+  auto xq = at::empty({a.M, a.K}, a.x2d.options().dtype(at::kFloat8_e4m3fn));
+  auto xs = at::empty({a.M}, a.x2d.options().dtype(at::kFloat));
+  if (a.M == 0) return {xq, xs};
+  check_rc(fp8lin_layernorm_modulate_quantize_fp8(
+               a.x2d.data_ptr(), dtype_code(a.x2d.scalar_type()), a.M, a.K, a.B,
+               a.shift.data_ptr(), a.scale.data_ptr(), static_cast<float>(eps), xq.data_ptr(),
+               xs.data_ptr<float>(), stream_of(a.x2d)),
+           "layernorm_modulate_quantize_fp8");
+  return {xq, xs};
+}
+
+at::Tensor fp8_linear_modulated(at::Tensor x, at::Tensor shift, at::Tensor scale, at::Tensor wq,
+                                at::Tensor w_scale, std::optional<at::Tensor> bias, double eps) {
+  c10::cuda::CUDAGuard guard(x.device());
+  ModArgs a = prep_modulation(x, shift, scale, "fp8_linear_modulated");
+  TORCH_CHECK(wq.is_cuda() && wq.scalar_type() == at::kFloat8_e4m3fn && wq.dim() == 2,
+              "fp8_linear_modulated: wq must be a 2D float8_e4m3fn CUDA tensor");
+  TORCH_CHECK(wq.size(1) == a.K, "K mismatch: x[..., K], wq[N, K]");
+  TORCH_CHECK(w_scale.scalar_type() == at::kFloat, "w_scale must be fp32");
+  auto wqc = aligned16(wq);
+  auto ws = w_scale.contiguous();
+  const int64_t N = wqc.size(0);
+  TORCH_CHECK(ws.numel() == N, "w_scale must have N entries (per-channel)");
+  auto out_shape = x.sizes().vec();
+  out_shape.back() = N;
+  auto out = at::empty({a.M, N}, a.x2d.options());
+  if (a.M > 0 && N > 0) {
+    BiasArg b = prep_bias(bias, N);
+    const size_t ws_bytes = fp8lin_linear_workspace_size(a.M, a.K);
+    auto workspace =
+        at::empty({static_cast<int64_t>(ws_bytes)}, a.x2d.options().dtype(at::kByte));
+    check_rc(fp8lin_fp8_linear_modulated(
+                 a.x2d.data_ptr(), dtype_code(a.x2d.scalar_type()), a.M, a.K, a.B,
+                 a.shift.data_ptr(), a.scale.data_ptr(), static_cast<float>(eps), wqc.data_ptr(),
+                 ws.data_ptr<float>(), b.ptr, b.dtype, out.data_ptr(),
+                 dtype_code(a.x2d.scalar_type()), N, workspace.data_ptr(), ws_bytes,
+                 stream_of(a.x2d)),
+             "fp8_linear_modulated");
+  }
+  return out.reshape(out_shape);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(fp8linear_b200, m) {
@@ -411,6 +489,10 @@ TORCH_LIBRARY(fp8linear_b200, m) {
   m.def("quantize_nvfp4(Tensor x) -> (Tensor, Tensor)");
   m.def("nvfp4_gemm(Tensor xq, Tensor x_scales, Tensor wq, Tensor w_scales, Tensor? bias) -> Tensor");
   m.def("nvfp4_linear(Tensor x, Tensor wq, Tensor w_scales, Tensor? bias) -> Tensor");
+  m.def("layernorm_modulate_quantize_fp8(Tensor x, Tensor shift, Tensor scale, float eps=1e-06) "
+        "-> (Tensor, Tensor)");
+  m.def("fp8_linear_modulated(Tensor x, Tensor shift, Tensor scale, Tensor wq, Tensor w_scale, "
+        "Tensor? bias, float eps=1e-06) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(fp8linear_b200, CUDA, m) {
@@ -424,4 +506,6 @@ TORCH_LIBRARY_IMPL(fp8linear_b200, CUDA, m) {
   m.impl("quantize_nvfp4", &quantize_nvfp4);
   m.impl("nvfp4_gemm", &nvfp4_gemm);
   m.impl("nvfp4_linear", &nvfp4_linear);
+  m.impl("layernorm_modulate_quantize_fp8", &layernorm_modulate_quantize_fp8);
+  m.impl("fp8_linear_modulated", &fp8_linear_modulated);
 }

@@ -139,6 +139,38 @@ def nvfp4_linear(x, wq, w_scales, bias=None):
     return ops.nvfp4_linear(x, wq, w_scales, bias)
 
 
+@torch.library.register_fake(add_op_namespace_prefix("layernorm_modulate_quantize_fp8"))
+def _layernorm_modulate_quantize_fp8_fake(x, shift, scale, eps=1e-6):
+    M = x.numel() // x.shape[-1]
+    xq = x.new_empty((M, x.shape[-1]), dtype=torch.float8_e4m3fn)
+    return xq, x.new_empty((M,), dtype=torch.float32)
+
+
+@torch.library.register_fake(add_op_namespace_prefix("fp8_linear_modulated"))
+def _fp8_linear_modulated_fake(x, shift, scale, wq, w_scale, bias=None, eps=1e-6):
+    return x.new_empty((*x.shape[:-1], wq.shape[0]), dtype=x.dtype)
+
+
+def layernorm_modulate_quantize_fp8(x, shift, scale, eps: float = 1e-6):
+    """The per-token e4m3 quantizer fused into the op that precedes the linear in a FLUX /
+    DiT block (AdaLayerNormZero): ``y = LayerNorm(x) * (1 + scale[b]) + shift[b]``
+    (LayerNorm without affine parameters, rounded to x's dtype after each step as the
+    unfused bf16 torch ops round it), quantized with ``quantize_fp8``'s rule, without ``y``
+    ever being written. ``x [B, T, K]`` (or ``[M, K]`` with B dividing M), ``shift`` and
+    ``scale [B, K]`` in x's dtype. Returns ``(xq e4m3 [M, K], x_scale fp32 [M])`` for
+    ``fp8_gemm``; no reference counterpart (it fuses the chain that feeds
+    ``Fp8Linear.forward``, layers.py:165-167 of the reference)."""
+    return ops.layernorm_modulate_quantize_fp8(x, shift, scale, eps)
+
+
+def fp8_linear_modulated(x, shift, scale, wq, w_scale, bias=None, eps: float = 1e-6):
+    """``fp8_linear(LayerNorm(x) * (1 + scale) + shift, wq, w_scale, bias)`` with the
+    modulated activations never in memory: the fused LayerNorm + modulation + quantizer,
+    then the FP8 GEMM with the dequant + bias epilogue. Returns ``[..., N]`` in x's
+    dtype."""
+    return ops.fp8_linear_modulated(x, shift, scale, wq, w_scale, bias, eps)
+
+
 def quantize_weight(weight: torch.Tensor):
     """Per-output-channel e4m3 quantization of a ``[N, K]`` CUDA weight (offline).
 

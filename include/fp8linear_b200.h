@@ -216,6 +216,42 @@ FP8LIN_API int fp8lin_nvfp4_linear(const void *x, int x_dtype, const void *wq,
                                    void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * The per-token quantizer fused into the op that precedes the linear in a FLUX / DiT
+ * block (AdaLayerNormZero modulation): for each row m of x (batch b = m / (M / batches))
+ *   y = LayerNorm(x[m]) * (1 + scale[b]) + shift[b]     (LayerNorm without affine, eps)
+ * rounded to x's type after each of the four steps as the unfused bf16/fp16 torch ops
+ * round it, then quantized exactly as fp8lin_quantize_fp8 quantizes y. y never goes to
+ * memory. No reference counterpart: it replaces, at the reference's call site
+ * (torch-ext/fp8linear/layers.py:165-167, the input of Fp8Linear.forward), the chain
+ * LayerNorm -> modulation -> quantize_fp8 (csrc/quantize.cu:199-234).
+ *   x      [M, K] x_dtype BF16 or F16, 16-byte aligned; K % 8 == 0, 8 <= K <= 8192
+ *   shift, scale [batches, K] of x_dtype, 16-byte aligned; batches divides M
+ *   xq [M, K] e4m3 codes; x_scale [M] fp32
+ * mean and variance are fp32 sums in a fixed order and rstd = 1 / sqrt(var + eps) with
+ * IEEE operations, so results are reproducible bit for bit (the CPU oracle restates the
+ * order). M == 0 is a no-op.
+ */
+FP8LIN_API int fp8lin_layernorm_modulate_quantize_fp8(const void *x, int x_dtype, int64_t M,
+                                                      int64_t K, int64_t batches,
+                                                      const void *shift, const void *scale,
+                                                      float eps, void *xq, float *x_scale,
+                                                      void *stream);
+
+/*
+ * fp8lin_layernorm_modulate_quantize_fp8 into the workspace (fp8lin_linear_workspace_size),
+ * then the FP8 GEMM with the fused dequant + bias epilogue launched as its programmatic
+ * dependent: out [M, N] = fp8_linear(y, wq, w_scale, bias) without y in memory. Arguments
+ * as fp8lin_layernorm_modulate_quantize_fp8 and fp8lin_fp8_linear.
+ */
+FP8LIN_API int fp8lin_fp8_linear_modulated(const void *x, int x_dtype, int64_t M, int64_t K,
+                                           int64_t batches, const void *shift,
+                                           const void *scale, float eps, const void *wq,
+                                           const float *w_scale, const void *bias,
+                                           int bias_dtype, void *out, int out_dtype,
+                                           int64_t N, void *workspace, size_t workspace_bytes,
+                                           void *stream);
+
+/*
  * Device workspace fp8lin_fp8_linear needs for M tokens of width K: the e4m3 codes
  * and the per-token scales of x (aligned sub-buffers).
  */

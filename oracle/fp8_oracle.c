@@ -28,6 +28,11 @@
  *                           (VEC16_UE4M3, bias epilogue, fp16 out; csrc/fp8_gemm.cu:347-446)
  *   oracle_mxfp8_gemm       cuBLASLt VEC32_UE8M0 block-scaled e4m3 matmul with the bias
  *                           epilogue, fp16 out (csrc/fp8_gemm.cu:233-333)
+ *   oracle_ln_modulate_quantize
+ *                           no reference function: the chain LayerNorm -> AdaLN modulation
+ *                           -> quantize_fp8 that feeds Fp8Linear.forward in a FLUX block
+ *                           (torch-ext/fp8linear/layers.py:165-167), in the fixed reduction
+ *                           order of the fused kernel, then oracle_quantize_rows' rule
  *
  * Arithmetic is IEEE binary32 with round-to-nearest-even and no flush-to-zero,
  * which is what nvcc emits for the reference without --use_fast_math.
@@ -77,6 +82,13 @@ uint16_t oracle_f32_to_f16(float f) {
   if (rem > 0x1000u || (rem == 0x1000u && (keep & 1u))) keep++;
   if (keep == 0x400u) { keep = 0; e++; }
   return (uint16_t)(s | (e << 10) | keep);
+}
+
+/* fp32 -> bf16 storage, round-to-nearest-even (__float2bfloat16_rn); NaN stays NaN. */
+uint16_t oracle_f32_to_bf16(float f) {
+  uint32_t u = f2u(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
 }
 
 /*
@@ -434,4 +446,75 @@ void oracle_nvfp4_gemm(const uint8_t *xq, const uint8_t *xs, const uint8_t *wq,
       out[m * N + n] = round_out ? oracle_f16_to_f32(oracle_f32_to_f16(v)) : v;
     }
   }
+}
+
+/*
+ * LayerNorm (no affine, eps) + modulation + per-token quantization, in the order of the
+ * fused kernel (fp8linear_b200's ln_mod_quant_kernel):
+ *   sum  = fp32 partial sums per lane l = 0..31 over the elements of its 8-element chunks
+ *          l, l + 32, l + 64, ... in sequence, then a butterfly over xor offsets
+ *          16, 8, 4, 2, 1 (lane l adds lane l^o's partial)
+ *   mean = sum / K; var = (same order over (x - mean)^2, a multiply then an add) / K
+ *   rstd = 1 / sqrtf(var + eps)
+ *   y    = R(R(R((x - mean) * rstd) * R(1 + scale[b])) + shift[b]), R = round to x's type
+ * then the rule of oracle_quantize_rows on y. Row r belongs to batch r / (M / batches);
+ * shift and scale are [batches, K] of x's type. dtype 0 = bf16, 1 = fp16.
+ */
+static float round_to(float v, int dtype) {
+  return dtype ? oracle_f16_to_f32(oracle_f32_to_f16(v)) : oracle_bf16_to_f32(oracle_f32_to_bf16(v));
+}
+
+static float lane_tree(float *part) {
+  float tmp[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    for (int l = 0; l < 32; ++l) tmp[l] = part[l] + part[l ^ o];
+    memcpy(part, tmp, sizeof(tmp));
+  }
+  return part[0];
+}
+
+void oracle_ln_modulate_quantize(const uint16_t *x, int dtype, int64_t M, int64_t K,
+                                 int64_t batches, const uint16_t *shift, const uint16_t *scale,
+                                 float eps, uint16_t *y, uint8_t *xq, float *xs) {
+  const int64_t nch = K / 8, rpb = M / batches;
+  for (int64_t r = 0; r < M; ++r) {
+    const uint16_t *row = x + r * K;
+    float part[32];
+    for (int l = 0; l < 32; ++l) {
+      part[l] = 0.0f;
+      for (int64_t c = l; c < nch; c += 32)
+        for (int e = 0; e < 8; ++e) {
+          float v = dtype ? oracle_f16_to_f32(row[8 * c + e]) : oracle_bf16_to_f32(row[8 * c + e]);
+          part[l] = part[l] + v;
+        }
+    }
+    volatile float mean = lane_tree(part) / (float)K;
+    for (int l = 0; l < 32; ++l) {
+      part[l] = 0.0f;
+      for (int64_t c = l; c < nch; c += 32)
+        for (int e = 0; e < 8; ++e) {
+          float v = dtype ? oracle_f16_to_f32(row[8 * c + e]) : oracle_bf16_to_f32(row[8 * c + e]);
+          volatile float d = v - mean;
+          volatile float dd = d * d;
+          part[l] = part[l] + dd;
+        }
+    }
+    volatile float var = lane_tree(part) / (float)K;
+    volatile float den = sqrtf(var + eps);
+    volatile float rstd = 1.0f / den;
+    const int64_t b = r / rpb;
+    uint16_t *yr = y + r * K;
+    for (int64_t j = 0; j < K; ++j) {
+      float v = dtype ? oracle_f16_to_f32(row[j]) : oracle_bf16_to_f32(row[j]);
+      float sc = dtype ? oracle_f16_to_f32(scale[b * K + j]) : oracle_bf16_to_f32(scale[b * K + j]);
+      float sh = dtype ? oracle_f16_to_f32(shift[b * K + j]) : oracle_bf16_to_f32(shift[b * K + j]);
+      volatile float dv = v - mean;
+      float ln = round_to(dv * rstd, dtype);
+      float m1 = round_to(1.0f + sc, dtype);
+      float t = round_to(ln * m1, dtype);
+      float yv = round_to(t + sh, dtype);
+      yr[j] = dtype ? oracle_f32_to_f16(yv) : oracle_f32_to_bf16(yv);
+    }
+  }
+  oracle_quantize_rows(y, dtype, M, K, xq, xs);
 }

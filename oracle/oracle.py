@@ -90,6 +90,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_quantize_nvfp4.restype = None
         L.oracle_nvfp4_gemm.argtypes = [P, P, P, P, P, i64, i64, i64, ctypes.c_int, P]
         L.oracle_nvfp4_gemm.restype = None
+        L.oracle_ln_modulate_quantize.argtypes = [P, ctypes.c_int, i64, i64, i64, P, P,
+                                                  ctypes.c_float, P, P, P]
+        L.oracle_ln_modulate_quantize.restype = None
         _lib = L
     return _lib
 
@@ -203,6 +206,22 @@ def c_nvfp4_gemm(xq, xs, wq, ws, bias16=None, round_out=True):
     return out
 
 
+def c_ln_modulate_quantize(x16, shift16, scale16, eps=1e-6, dtype: int = BF16):
+    """LayerNorm + AdaLN modulation + per-token quantization (oracle_ln_modulate_quantize).
+    x16 uint16 [M, K]; shift16 / scale16 uint16 [B, K] (B divides M). Returns
+    (y uint16 [M, K], xq uint8 [M, K], xs float32 [M])."""
+    x16 = np.ascontiguousarray(x16, np.uint16)
+    shift16 = np.ascontiguousarray(shift16, np.uint16)
+    scale16 = np.ascontiguousarray(scale16, np.uint16)
+    M, K = x16.shape
+    y = np.empty((M, K), np.uint16)
+    xq = np.empty((M, K), np.uint8)
+    xs = np.empty((M,), np.float32)
+    lib().oracle_ln_modulate_quantize(_ptr(x16), dtype, M, K, shift16.shape[0], _ptr(shift16),
+                                      _ptr(scale16), float(eps), _ptr(y), _ptr(xq), _ptr(xs))
+    return y, xq, xs
+
+
 def c_e4m3_encode(v: float, saturate: bool = True) -> int:
     return int(lib().oracle_e4m3_encode(float(v), int(saturate)))
 
@@ -294,6 +313,56 @@ def np_quantize_rows(x16: np.ndarray, dtype: int = BF16):
         p = (xf * inv[:, None]).astype(np.float32)
     c = np.fmin(np.fmax(p, -E4M3_MAX), E4M3_MAX)
     return np_e4m3_encode(c, saturate=True), sc
+
+
+def _np_round_to(f: np.ndarray, dtype: int) -> np.ndarray:
+    f = np.ascontiguousarray(f, np.float32)
+    if dtype == BF16:
+        return bf16_bits_to_f32(f32_to_bf16_bits(f))
+    return f.astype(np.float16).astype(np.float32)
+
+
+def _np_lane_tree(part: np.ndarray) -> np.ndarray:
+    idx = np.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        part = (part + part[:, idx ^ o]).astype(np.float32)
+    return part[:, 0]
+
+
+def np_ln_modulate_quantize(x16, shift16, scale16, eps=1e-6, dtype: int = BF16):
+    """Vectorised twin of oracle_ln_modulate_quantize (bit-identical)."""
+    x16 = np.ascontiguousarray(x16, np.uint16)
+    M, K = x16.shape
+    B = shift16.shape[0]
+    to32 = bf16_bits_to_f32 if dtype == BF16 else f16_bits_to_f32
+    xf = to32(x16)
+    nch = K // 8
+    chunks = xf.reshape(M, nch, 8)
+    kf = np.float32(K)
+
+    def lane_sums(vals):  # vals [M, nch, 8] float32 -> lane partials [M, 32]
+        part = np.zeros((M, 32), np.float32)
+        for i in range(-(-nch // 32)):
+            lo, hi = 32 * i, min(32 * i + 32, nch)
+            for e in range(8):
+                part[:, : hi - lo] = (part[:, : hi - lo] + vals[:, lo:hi, e]).astype(np.float32)
+        return part
+
+    with np.errstate(invalid="ignore", over="ignore"):
+        mean = (_np_lane_tree(lane_sums(chunks)) / kf).astype(np.float32)
+        d = (chunks - mean[:, None, None]).astype(np.float32)
+        var = (_np_lane_tree(lane_sums((d * d).astype(np.float32))) / kf).astype(np.float32)
+        rstd = (np.float32(1.0) / np.sqrt((var + np.float32(eps)).astype(np.float32))).astype(np.float32)
+        b = np.arange(M) // (M // B)
+        sc = to32(np.ascontiguousarray(scale16, np.uint16))[b]
+        sh = to32(np.ascontiguousarray(shift16, np.uint16))[b]
+        ln = _np_round_to(((xf - mean[:, None]).astype(np.float32) * rstd[:, None]).astype(np.float32), dtype)
+        m1 = _np_round_to((np.float32(1.0) + sc).astype(np.float32), dtype)
+        t = _np_round_to((ln * m1).astype(np.float32), dtype)
+        y = _np_round_to((t + sh).astype(np.float32), dtype)
+    y16 = f32_to_bf16_bits(y) if dtype == BF16 else y.astype(np.float16).view(np.uint16)
+    xq, xs = np_quantize_rows(y16, dtype)
+    return y16, xq, xs
 
 
 def np_quantize_weight(w: np.ndarray, dtype: int = BF16, recip_scalar: bool = True):
