@@ -792,22 +792,39 @@ cudaError_t launch_mx_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, ui
 // One warp per row holding the row in registers (K <= 8192, K % 8 == 0); 8 rows per CTA.
 constexpr int kLnThreads = 256;
 
+// Pairs of values: IEEE fp32 add / multiply of two lanes at once, and rounding of a pair to
+// T (round-to-nearest-even, one convert) with the rounded values read back exactly.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 r;
+  asm("{.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2v(float2 a, float2 b) {
+  float2 r;
+  asm("{.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
 template <typename T>
 struct Rnd;
 template <>
 struct Rnd<__nv_bfloat16> {
-  __device__ __forceinline__ static uint32_t bits(float v) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  __device__ __forceinline__ static uint32_t pack(float2 v) { return ptx::pack_bf16x2(v.x, v.y); }
+  __device__ __forceinline__ static float2 unpack(uint32_t b) {
+    return make_float2(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
   }
-  __device__ __forceinline__ static float val(uint32_t b) { return __uint_as_float(b << 16); }
 };
 template <>
 struct Rnd<__half> {
-  __device__ __forceinline__ static uint32_t bits(float v) {
-    return __half_as_ushort(__float2half_rn(v));
-  }
-  __device__ __forceinline__ static float val(uint32_t b) {
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+  __device__ __forceinline__ static uint32_t pack(float2 v) { return ptx::pack_f16x2(v.x, v.y); }
+  __device__ __forceinline__ static float2 unpack(uint32_t b) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&b));
   }
 };
 
@@ -846,49 +863,65 @@ __global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
     }
   }
   const float mean = __fdiv_rn(warp_sum_xor(sum), kf);
+  // (x - mean)^2 two elements at a time (x - mean is x + (-mean): the same IEEE result),
+  // accumulated in element order
+  const float2 nmean = make_float2(-mean, -mean);
   float sq = 0.0f;
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {
     if (lane + 32 * i < nch) {
-      float f[8];
-      In<T>::unpack8(v[i], f);
+      const uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float d = __fsub_rn(f[e], mean);
-        sq = __fadd_rn(sq, __fmul_rn(d, d));
+      for (int p = 0; p < 4; ++p) {
+        const float2 d = add2(Rnd<T>::unpack(xw[p]), nmean);
+        const float2 dd = mul2v(d, d);
+        sq = __fadd_rn(sq, dd.x);
+        sq = __fadd_rn(sq, dd.y);
       }
     }
   }
   const float var = __fdiv_rn(warp_sum_xor(sq), kf);
   const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
   const int64_t boff = (row / rows_per_batch) * static_cast<int64_t>(K);
-  float amax = 0.0f;
+  // y, two elements at a time
+  const float2 rs2 = make_float2(rstd, rstd);
+  const float2 one2 = make_float2(1.0f, 1.0f);
+  uint32_t mag = 0;  // packed max of |y| bit patterns (the amax of finite rows)
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {
     const int c = lane + 32 * i;
     if (c < nch) {
-      float f[8], fs[8], fh[8];
-      In<T>::unpack8(v[i], f);
-      In<T>::unpack8(__ldg(reinterpret_cast<const uint4 *>(scale + boff + 8 * c)), fs);
-      In<T>::unpack8(__ldg(reinterpret_cast<const uint4 *>(shift + boff + 8 * c)), fh);
+      const uint4 sv = __ldg(reinterpret_cast<const uint4 *>(scale + boff + 8 * c));
+      const uint4 hv = __ldg(reinterpret_cast<const uint4 *>(shift + boff + 8 * c));
+      const uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
       uint32_t w[4];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        uint32_t b2[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float ln = Rnd<T>::val(Rnd<T>::bits(__fmul_rn(__fsub_rn(f[e + h], mean), rstd)));
-          const float m1 = Rnd<T>::val(Rnd<T>::bits(__fadd_rn(1.0f, fs[e + h])));
-          const float t = Rnd<T>::val(Rnd<T>::bits(__fmul_rn(ln, m1)));
-          b2[h] = Rnd<T>::bits(__fadd_rn(t, fh[e + h]));
-          amax = fmaxf(amax, fabsf(Rnd<T>::val(b2[h])));
-        }
-        w[e >> 1] = b2[0] | (b2[1] << 16);
+      for (int p = 0; p < 4; ++p) {
+        const float2 ln = Rnd<T>::unpack(Rnd<T>::pack(mul2v(add2(Rnd<T>::unpack(xw[p]), nmean), rs2)));
+        const float2 m1 = Rnd<T>::unpack(Rnd<T>::pack(add2(one2, Rnd<T>::unpack(sw[p]))));
+        const float2 t = Rnd<T>::unpack(Rnd<T>::pack(mul2v(ln, m1)));
+        w[p] = Rnd<T>::pack(add2(t, Rnd<T>::unpack(hw[p])));
+        mag = mag_max2(mag, w[p]);
       }
       v[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
-  amax = warp_max(amax);
+  // quantize_fp8's rule on y: the packed-integer amax and the fast conversion when the row
+  // is finite, the float amax (NaN ignored) and the literal clamp otherwise
+  const uint32_t mmax = fold_halves(mag);
+  const bool finite = __all_sync(0xffffffffu, mmax <= Bits<T>::kMaxFinite);
+  float amax;
+  if (finite) {
+    amax = warp_max(Bits<T>::to_float(mmax));
+  } else {
+    amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i)
+      if (lane + 32 * i < nch) amax = amax8_float<T>(amax, v[i]);
+    amax = warp_max(amax);
+  }
   const float sc = fmaxf(__fdiv_rn(amax, kE4M3Max), kScaleFloor);
   const float inv = __fdiv_rn(1.0f, sc);
   if (lane == 0) xs[row] = sc;
@@ -896,7 +929,9 @@ __global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {
     const int c = lane + 32 * i;
-    if (c < nch) *reinterpret_cast<uint2 *>(qr + 8 * c) = quant8_clamp<T>(v[i], inv);
+    if (c < nch)
+      *reinterpret_cast<uint2 *>(qr + 8 * c) =
+          finite ? quant8_fast<T>(v[i], inv) : quant8_clamp<T>(v[i], inv);
   }
 }
 
