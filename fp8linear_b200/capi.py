@@ -34,6 +34,8 @@ SIGNATURES = {
     "fp8lin_layernorm_modulate_quantize_fp8": (_I, [_P, _I, _I64, _I64, _I64, _P, _P, _F, _P, _P, _P]),
     "fp8lin_fp8_linear_modulated": (_I, [_P, _I, _I64, _I64, _I64, _P, _P, _F, _P, _P, _P, _I, _P,
                                         _I, _I64, _P, _SZ, _P]),
+    "fp8lin_fp8_linear_host_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "fp8lin_fp8_linear_host": (_I, [_P, _I, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P, _SZ, _P]),
     "fp8lin_nv_scale_bytes": (_SZ, [_I64, _I64]),
     "fp8lin_quantize_nvfp4": (_I, [_P, _I, _I64, _I64, _P, _P, _P]),
     "fp8lin_nvfp4_gemm": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I64, _I64, _I64, _P]),
@@ -205,6 +207,26 @@ class CApi:
             workspace.numel(), self._stream(x))
         self._check(rc, "fp8lin_fp8_linear_modulated")
         return out
+
+    def fp8_linear_host(self, x_host, wq, w_scale, bias=None, out_host=None, out_dtype=None,
+                        workspace=None):
+        """x_host / out_host in (pinned) host memory; weights on the device. Queued on the
+        current stream of wq's device; synchronize it before reading out_host."""
+        M, K = x_host.shape
+        N = wq.shape[0]
+        out_dtype = x_host.dtype if out_dtype is None else out_dtype
+        if out_host is None:
+            out_host = torch.empty((M, N), dtype=out_dtype, pin_memory=True)
+        need = int(self.lib.fp8lin_fp8_linear_host_workspace_size(M, N, K))
+        if workspace is None:
+            workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=wq.device)
+        rc = self.lib.fp8lin_fp8_linear_host(x_host.data_ptr(), DTYPE[x_host.dtype], wq.data_ptr(),
+                                             w_scale.data_ptr(), self._bias_ptr(bias),
+                                             self._bias_dtype(bias), out_host.data_ptr(),
+                                             DTYPE[out_host.dtype], M, N, K, workspace.data_ptr(),
+                                             workspace.numel(), self._stream(wq))
+        self._check(rc, "fp8lin_fp8_linear_host")
+        return out_host
 
     def quantize_weight(self, w: torch.Tensor):
         N, K = w.shape

@@ -454,6 +454,140 @@ int fp8lin_fp8_linear_modulated(const void *x, int x_dtype, int64_t M, int64_t K
   return launch_gemm(a, s, true);
 }
 
+// ---------------------------------------------------------------- host-buffer linear
+namespace {
+constexpr int64_t kHostChunkRows = 512;
+
+struct HostStreams {
+  bool ready = false;
+  cudaError_t err = cudaSuccess;
+  cudaStream_t up = nullptr, comp = nullptr, down = nullptr;
+  cudaEvent_t start = nullptr, up_done[2] = {}, comp_done[2] = {}, down_done[2] = {};
+};
+
+// The three streams and the events of the current device (created once, kept for the
+// life of the process).
+HostStreams *host_streams(std::string *why) {
+  static std::mutex mu;
+  static HostStreams hs[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *why = cudaGetErrorString(e);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  HostStreams &h = hs[dev & 63];
+  if (!h.ready) {
+    h.ready = true;
+    const unsigned sf = cudaStreamNonBlocking;
+    const unsigned ef = cudaEventDisableTiming;
+    if ((h.err = cudaStreamCreateWithFlags(&h.up, sf)) == cudaSuccess &&
+        (h.err = cudaStreamCreateWithFlags(&h.comp, sf)) == cudaSuccess &&
+        (h.err = cudaStreamCreateWithFlags(&h.down, sf)) == cudaSuccess &&
+        (h.err = cudaEventCreateWithFlags(&h.start, ef)) == cudaSuccess) {
+      for (int i = 0; i < 2 && h.err == cudaSuccess; ++i)
+        if ((h.err = cudaEventCreateWithFlags(&h.up_done[i], ef)) == cudaSuccess &&
+            (h.err = cudaEventCreateWithFlags(&h.comp_done[i], ef)) == cudaSuccess)
+          h.err = cudaEventCreateWithFlags(&h.down_done[i], ef);
+    }
+  }
+  if (h.err != cudaSuccess) {
+    *why = cudaGetErrorString(h.err);
+    return nullptr;
+  }
+  return &h;
+}
+
+int64_t host_chunk_rows(int64_t M) { return M < kHostChunkRows ? M : kHostChunkRows; }
+}  // namespace
+
+size_t fp8lin_fp8_linear_host_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int64_t c = host_chunk_rows(M);
+  // two x chunks (2 B per element), two out chunks (2 B), one quantizer workspace
+  return 2 * round_up(static_cast<size_t>(c * K * 2), kWsAlign) +
+         2 * round_up(static_cast<size_t>(c * N * 2), kWsAlign) + fp8lin_linear_workspace_size(c, K);
+}
+
+int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, const float *w_scale,
+                           const void *bias, int bias_dtype, void *out_host, int out_dtype,
+                           int64_t M, int64_t N, int64_t K, void *workspace,
+                           size_t workspace_bytes, void *stream) {
+  clear_error();
+  if (x_dtype != kBF16 && x_dtype != kF16)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear_host: x must be fp16 or bf16");
+  int rc = check_gemm_args(reinterpret_cast<const void *>(16), w_scale, wq, w_scale, bias,
+                           bias_dtype, reinterpret_cast<const void *>(16), out_dtype, M, N, K,
+                           "fp8_linear_host");
+  if (rc != FP8LIN_OK || M == 0 || N == 0) return rc;
+  if (!x_host || !out_host) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "fp8_linear_host: null host buffer");
+  const size_t need = fp8lin_fp8_linear_host_workspace_size(M, N, K);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, kWsAlign))
+    return fail(FP8LIN_ERR_WORKSPACE, "fp8_linear_host: workspace of " + std::to_string(need) +
+                                          " bytes (256-byte aligned) required, got " +
+                                          std::to_string(workspace_bytes));
+  std::string why;
+  HostStreams *h = host_streams(&why);
+  if (!h) return fail(FP8LIN_ERR_CUDA, "fp8_linear_host: stream setup: " + why);
+  const int64_t rows = host_chunk_rows(M);
+  const size_t xb = round_up(static_cast<size_t>(rows * K * 2), kWsAlign);
+  const size_t ob = round_up(static_cast<size_t>(rows * N * 2), kWsAlign);
+  uint8_t *base = static_cast<uint8_t *>(workspace);
+  uint8_t *xbuf[2] = {base, base + xb};
+  uint8_t *obuf[2] = {base + 2 * xb, base + 2 * xb + ob};
+  uint8_t *xq = base + 2 * xb + 2 * ob;
+  float *xs = reinterpret_cast<float *>(xq + round_up(static_cast<size_t>(rows * K), kWsAlign));
+  cudaStream_t user = static_cast<cudaStream_t>(stream);
+  const char *step = "ordering";
+  cudaError_t e = cudaEventRecord(h->start, user);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(h->up, h->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(h->comp, h->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(h->down, h->start, 0);
+  const int64_t chunks = (M + rows - 1) / rows;
+  for (int64_t i = 0; i < chunks && e == cudaSuccess; ++i) {
+    const int s = static_cast<int>(i & 1);
+    const int64_t r0 = i * rows;
+    const int64_t mr = M - r0 < rows ? M - r0 : rows;
+    // upload chunk i once the kernels of chunk i-2 no longer read this x slot
+    step = "upload";
+    if (i >= 2) e = cudaStreamWaitEvent(h->up, h->comp_done[s], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(xbuf[s], static_cast<const uint8_t *>(x_host) + r0 * K * 2,
+                          static_cast<size_t>(mr * K * 2), cudaMemcpyHostToDevice, h->up);
+    if (e == cudaSuccess) e = cudaEventRecord(h->up_done[s], h->up);
+    // kernels of chunk i once it has landed and chunk i-2's output has left this slot
+    step = "kernels";
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(h->comp, h->up_done[s], 0);
+    if (e == cudaSuccess && i >= 2) e = cudaStreamWaitEvent(h->comp, h->down_done[s], 0);
+    if (e != cudaSuccess) break;
+    e = launch_quantize_rows(xbuf[s], x_dtype, mr, K, xq, xs, h->comp, true);
+    if (e != cudaSuccess) break;
+    GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
+               bias ? bias_dtype : kNone, obuf[s], out_dtype, mr, N, K};
+    rc = launch_gemm(a, h->comp, true);
+    if (rc != FP8LIN_OK) return rc;  // launch_gemm set the message
+    e = cudaEventRecord(h->comp_done[s], h->comp);
+    // download chunk i
+    step = "download";
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(h->down, h->comp_done[s], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(static_cast<uint8_t *>(out_host) + r0 * N * 2, obuf[s],
+                          static_cast<size_t>(mr * N * 2), cudaMemcpyDeviceToHost, h->down);
+    if (e == cudaSuccess) e = cudaEventRecord(h->down_done[s], h->down);
+  }
+  // the caller's stream continues once the last download is done (it follows every
+  // earlier copy and kernel of the call)
+  if (e == cudaSuccess) {
+    step = "ordering";
+    e = cudaStreamWaitEvent(user, h->down_done[(chunks - 1) & 1], 0);
+  }
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("fp8_linear_host: ") + step + ": " +
+                                     cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
 int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, const float *w_scale,
                                 const void *bias, int bias_dtype, void *const *outs, int n_outs,
                                 int out_dtype, int64_t M, int64_t N, int64_t K, int64_t ldo,

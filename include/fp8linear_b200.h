@@ -252,6 +252,24 @@ FP8LIN_API int fp8lin_fp8_linear_modulated(const void *x, int x_dtype, int64_t M
                                            void *stream);
 
 /*
+ * fp8lin_fp8_linear with x and out in host memory (page-locked for the copies to be
+ * asynchronous): the path of a host that keeps activations in its own memory. Rows go in
+ * chunks of up to 512; the upload of chunk i+1, the quantizer + GEMM of chunk i and the
+ * download of chunk i-1 run on three streams of the library's own, so PCIe carries both
+ * directions at once and the kernels hide behind the copies. The work is ordered after
+ * what is already queued on `stream`, and `stream` waits for its end: synchronize
+ * `stream` before reading out. wq, w_scale and bias are device pointers as in
+ * fp8lin_fp8_linear. Replaces the host-side copies around the reference's fp8_linear
+ * (csrc/fp8_gemm.cu:196-221), which takes device tensors only.
+ */
+FP8LIN_API size_t fp8lin_fp8_linear_host_workspace_size(int64_t M, int64_t N, int64_t K);
+FP8LIN_API int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq,
+                                      const float *w_scale, const void *bias, int bias_dtype,
+                                      void *out_host, int out_dtype, int64_t M, int64_t N,
+                                      int64_t K, void *workspace, size_t workspace_bytes,
+                                      void *stream);
+
+/*
  * Device workspace fp8lin_fp8_linear needs for M tokens of width K: the e4m3 codes
  * and the per-token scales of x (aligned sub-buffers).
  */
