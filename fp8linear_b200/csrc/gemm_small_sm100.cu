@@ -47,7 +47,11 @@ constexpr uint32_t X_STAGE_MAX = MAX_TOK * BK;            // 16 KB
 constexpr uint32_t STAGE_MAX = W_STAGE + X_STAGE_MAX;
 constexpr uint32_t PART_MAX = MAX_TOK * WN * 4;           // fp32 partial tile, 64 KB
 constexpr uint32_t OFF_PART = STAGES * STAGE_MAX;         // 128 KB
-constexpr uint32_t OFF_BAR = OFF_PART + PART_MAX;
+// the reduction's operands that do not depend on the partials: x_scale of every token,
+// w_scale and bias of this CTA's rows (staged before the cluster barrier)
+constexpr uint32_t OFF_EPI = OFF_PART + PART_MAX;
+constexpr uint32_t EPI_BYTES = (MAX_TOK + 2 * WN) * 4;
+constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + (2 * STAGES + 2) * 8 + 16 + 1024;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint64_t kDrainLimitNs = 1000000000ull;
@@ -223,17 +227,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::tc_fence_before();
   }
 
-  __syncwarp();
-  __syncthreads();
-  ptx::cluster_sync();  // every CTA's partial tile is in its shared memory
-
   // CTA `rank` reduces tile rows [r0, r1) (a multiple of 4 wide) over the cluster's
-  // partials and writes out. Each task is 4 consecutive rows of one token: the loads from
-  // all ranks' shared memory are issued together, then summed in rank order.
+  // partials and writes out. Stage what that needs besides the partials first, so that
+  // its global-memory latency overlaps the cluster barrier.
   const int R = ((WN + p.split - 1) / p.split + 3) & ~3;
   const int r0 = static_cast<int>(rank) * R;
   const int r1 = min(WN, r0 + R);
   const int quads = r1 > r0 ? (r1 - r0) >> 2 : 0;
+  float *e_xs = reinterpret_cast<float *>(smem + OFF_EPI);  // [MAX_TOK]
+  float *e_ws = e_xs + MAX_TOK;                              // [WN]: rows r0.. of the tile
+  float *e_b = e_ws + WN;
+  for (int i = threadIdx.x; i < p.M; i += NUM_THREADS) e_xs[i] = __ldg(p.xs + i);
+  for (int i = threadIdx.x; i < r1 - r0; i += NUM_THREADS) {
+    const int n = tile * WN + r0 + i;
+    const bool in = n < p.N;
+    e_ws[i] = in ? __ldg(p.ws + n) : 0.0f;
+    e_b[i] = in && p.bias_dtype != kNone ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
+  }
+
+  __syncwarp();
+  __syncthreads();
+  ptx::cluster_sync();  // every CTA's partial tile is in its shared memory
+
+  // Each task is 4 consecutive rows of one token: the loads from all ranks' shared memory
+  // are issued together, then summed in rank order.
   const uint32_t part_base = ptx::smem_u32(part);
   for (int idx = threadIdx.x; idx < p.M * quads; idx += NUM_THREADS) {
     const int m = idx / quads;
@@ -252,13 +269,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         acc[2] += v[s2].z;
         acc[3] += v[s2].w;
       }
-    const float xs = __ldg(p.xs + m);
+    const float xs = e_xs[m];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int n = tile * WN + nl + e;
       if (n >= p.N) break;
-      const float val = fmaf(acc[e] * xs, __ldg(p.ws + n),
-                             p.bias_dtype != kNone ? load_bias(p.bias, p.bias_dtype, n) : 0.0f);
+      const float val = fmaf(acc[e] * xs, e_ws[nl - r0 + e], e_b[nl - r0 + e]);
       const int64_t o = static_cast<int64_t>(m) * p.ldo + n;
       if (p.out_dtype == kF16)
         reinterpret_cast<__half *>(p.out)[o] = __float2half_rn(val);
