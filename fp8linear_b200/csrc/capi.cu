@@ -459,6 +459,7 @@ namespace {
 constexpr int64_t kHostChunkRows = 512;
 
 struct HostStreams {
+  std::mutex enqueue;  // one call's copies, kernels and event records at a time
   bool ready = false;
   cudaError_t err = cudaSuccess;
   cudaStream_t up = nullptr, comp = nullptr, down = nullptr;
@@ -539,6 +540,9 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
   uint8_t *xq = base + 2 * xb + 2 * ob;
   float *xs = reinterpret_cast<float *>(xq + round_up(static_cast<size_t>(rows * K), kWsAlign));
   cudaStream_t user = static_cast<cudaStream_t>(stream);
+  // Calls from several host threads share the device's streams and events: the event
+  // records and waits of one call must not interleave with another's.
+  std::lock_guard<std::mutex> serial(h->enqueue);
   const char *step = "ordering";
   cudaError_t e = cudaEventRecord(h->start, user);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(h->up, h->start, 0);

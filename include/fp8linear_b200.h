@@ -258,7 +258,8 @@ FP8LIN_API int fp8lin_fp8_linear_modulated(const void *x, int x_dtype, int64_t M
  * download of chunk i-1 run on three streams of the library's own, so PCIe carries both
  * directions at once and the kernels hide behind the copies. The work is ordered after
  * what is already queued on `stream`, and `stream` waits for its end: synchronize
- * `stream` before reading out. wq, w_scale and bias are device pointers as in
+ * `stream` before reading out. Calls on one device from several host threads are
+ * queued one after another. wq, w_scale and bias are device pointers as in
  * fp8lin_fp8_linear. Replaces the host-side copies around the reference's fp8_linear
  * (csrc/fp8_gemm.cu:196-221), which takes device tensors only.
  */
