@@ -71,3 +71,27 @@ def test_host_linear_workspace_checked(capi):
     small = torch.empty(1024, dtype=torch.uint8, device="cuda")
     with pytest.raises(RuntimeError, match="workspace"):
         capi.fp8_linear_host(x, wq, ws, b, workspace=small)
+
+
+def test_host_linear_concurrent_callers(capi):
+    """Several host threads calling at once on one device (ctypes drops the GIL): each
+    call keeps its own chunks apart from the others' on the shared streams."""
+    import threading
+
+    wq, ws, b = _weights(512, 1024, seed=9)
+    xs = [torch.randn(1500, 1024, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    want = [capi.fp8_linear(x.cuda(), wq, ws, b).cpu() for x in xs]
+    outs = [None] * len(xs)
+
+    def run(i):
+        outs[i] = capi.fp8_linear_host(xs[i], wq, ws, b)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        ts = [threading.Thread(target=run, args=(i,)) for i in range(len(xs))]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        for i in range(len(xs)):
+            assert torch.equal(outs[i], want[i]), i
