@@ -474,10 +474,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int j4 = 0; j4 < EPI_COLS / 4; ++j4) {
           const float4 w = w4[j4];
           const float4 bb = b4[j4];
-          const float v0 = fmaf(__uint_as_float(r[4 * j4 + 0]) * xs, w.x, bb.x);
-          const float v1 = fmaf(__uint_as_float(r[4 * j4 + 1]) * xs, w.y, bb.y);
-          const float v2 = fmaf(__uint_as_float(r[4 * j4 + 2]) * xs, w.z, bb.z);
-          const float v3 = fmaf(__uint_as_float(r[4 * j4 + 3]) * xs, w.w, bb.w);
+          // fmaf(acc * x_scale, w_scale, bias), two columns per instruction
+          const float2 v01 = ptx::mul_fma2(
+              make_float2(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1])), xs,
+              make_float2(w.x, w.y), make_float2(bb.x, bb.y));
+          const float2 v23 = ptx::mul_fma2(
+              make_float2(__uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3])), xs,
+              make_float2(w.z, w.w), make_float2(bb.z, bb.w));
+          const float v0 = v01.x, v1 = v01.y, v2 = v23.x, v3 = v23.y;
           if (p.out_dtype == kF16) {
             packed[2 * j4] = ptx::pack_f16x2(v0, v1);
             packed[2 * j4 + 1] = ptx::pack_f16x2(v2, v3);

@@ -499,6 +499,18 @@ __device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
   return r;
 }
 
+// (a.x * s, a.y * s) then that times w plus b, two lanes at a time: one IEEE multiply and
+// one fused multiply-add per element, the same results as fmaf(a * s, w, b).
+__device__ __forceinline__ float2 mul_fma2(float2 a, float s, float2 w, float2 b) {
+  float2 r;
+  asm("{.reg .b64 x, y, z, t, u, v;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %4};\n\t"
+      "mul.rn.f32x2 t, x, y;\n\tmov.b64 z, {%5, %6};\n\tmov.b64 u, {%7, %8};\n\t"
+      "fma.rn.f32x2 v, t, z, u;\n\tmov.b64 {%0, %1}, v;}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(s), "f"(w.x), "f"(w.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
