@@ -140,3 +140,24 @@ def test_argument_checks():
     with pytest.raises(RuntimeError, match="8192"):
         big = torch.zeros(2, 8200, device="cuda", dtype=torch.bfloat16)
         f.layernorm_modulate_quantize_fp8(big, big[:1], big[:1])
+
+
+@pytest.mark.parametrize("M,B", [(1, 1), (16, 2), (100, 4), (128, 1)])
+def test_fused_linear_few_tokens(M, B):
+    """Few tokens take the split-K few-token GEMM as the quantizer's PDL dependent: the
+    fused modulated linear equals quantize + GEMM bit for bit there too."""
+    import fp8linear_b200 as f
+
+    K, N = 1024, 768
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = f.quantize_weight(w)
+    shift, scale = _mod(B, K, torch.bfloat16, seed=M + 1)
+    out = f.fp8_linear_modulated(x, shift, scale, wq, ws, b)
+    xq, xs = f.layernorm_modulate_quantize_fp8(x, shift, scale)
+    two = f.fp8_gemm(xq, xs, wq, ws, b)
+    torch.cuda.synchronize()
+    assert out.shape == (M, N)
+    assert torch.equal(out, two)
