@@ -810,6 +810,14 @@ bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_
                             box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_128B, err);
 }
 
+// A tiled scale grid of `rows` rows as [row blocks][ncb tiles][128 words]; a box is
+// `tiles_per_box` consecutive tiles of one row block.
+bool make_tmap_sf(CUtensorMap *map, const void *base, uint64_t rows, uint64_t ncb,
+                  uint32_t tiles_per_box, std::string *err) {
+  return gemm::make_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, base, 128, ncb,
+                            (rows + 127) / 128, 512, ncb * 512, 128, tiles_per_box, err);
+}
+
 int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   if (a.M == 0 || a.N == 0) return 0;
   DeviceInfo dev;
@@ -824,17 +832,14 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     set_error("fp8_gemm: dimensions must fit in int32 and at most 7 peers");
     return 2;
   }
-  // MXFP8 / NVFP4: single CTAs with 128-row tiles for M <= 128, CTA pairs otherwise.
+  // MXFP8 / NVFP4: the few-token kernel for M <= 128, CTA pairs otherwise.
   if (a.mx) {
     if (a.n_peers != 0) {
       set_error("block-scaled gemm: peer outputs are not supported");
       return 2;
     }
-    if (a.nv) {
-      if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtNV>(a, dev, stream, pdl);
-      return gemm::launch_shape<2, gemm::kFmtNV>(a, dev, stream, pdl);
-    }
-    if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtMX>(a, dev, stream, pdl);
+    if (a.M <= gemm::BM) return launch_gemm_small(a, stream, pdl);
+    if (a.nv) return gemm::launch_shape<2, gemm::kFmtNV>(a, dev, stream, pdl);
     return gemm::launch_shape<2, gemm::kFmtMX>(a, dev, stream, pdl);
   }
   // Few tokens: stream the weights with swap-AB split-K tiles. Otherwise CTA pairs with

@@ -18,6 +18,16 @@
 // owner), warps 2-5 move the accumulator from TMEM to shared memory; all warps reduce.
 // Every mbarrier wait is bounded; a wait that runs out sets bit 16 of this file's
 // watchdog word (read with the others by fp8lin_device_status) and the CTA winds down.
+//
+// The block-scaled forms (template parameter F: MXFP8, e4m3 codes with an e8m0 scale per
+// 32 K-elements; NVFP4, e2m1 codes two per byte with a ue4m3 scale per 16) keep the same
+// tiling, byte for byte along K (a K-block is 128 bytes of a row), and add to each stage
+// the K-block's scale tiles in the quantizers' tiled layout (512-byte tiles of 128 rows x
+// 4 scales): 1 (MX) or 4 (NV) tiles of the weight tile's 128 rows and as many of token
+// rows 0-127. Before the K-block's MMAs they are copied into TMEM after the accumulator
+// (tcgen05.cp .32x128b.warpx4, 4 columns per tile; weight scales are the MMA's scale A,
+// token scales its scale B, of which an MMA with N = padded tokens reads rows 0..N-1). The
+// scales are inside the accumulator, so the reduction adds only the bias.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -44,18 +54,31 @@ constexpr int STAGES = 4;
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t W_STAGE = WN * BK;                     // 16 KB
 constexpr uint32_t X_STAGE_MAX = MAX_TOK * BK;            // 16 KB
-constexpr uint32_t STAGE_MAX = W_STAGE + X_STAGE_MAX;
 constexpr uint32_t PART_MAX = MAX_TOK * WN * 4;           // fp32 partial tile, 64 KB
-constexpr uint32_t OFF_PART = STAGES * STAGE_MAX;         // 128 KB
 // the reduction's operands that do not depend on the partials: x_scale of every token,
 // w_scale and bias of this CTA's rows (staged before the cluster barrier)
-constexpr uint32_t OFF_EPI = OFF_PART + PART_MAX;
 constexpr uint32_t EPI_BYTES = (MAX_TOK + 2 * WN) * 4;
-constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
-constexpr uint32_t SMEM_BYTES = OFF_BAR + (2 * STAGES + 2) * 8 + 16 + 1024;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint64_t kDrainLimitNs = 1000000000ull;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+// Operand formats, numbered as the large kernel's.
+enum : int { kFmtE4M3 = 0, kFmtMX = 1, kFmtNV = 2 };
+
+template <int F>
+struct Cfg {
+  static constexpr bool BS = F != kFmtE4M3;  // block-scaled
+  static constexpr bool NV = F == kFmtNV;
+  static constexpr int SF_TILES = NV ? 4 : BS ? 1 : 0;   // scale tiles per K-block and operand
+  static constexpr uint32_t SF_STAGE = 512u * SF_TILES;
+  // stage: [weight 16 KB][tokens mpad x 128 B][weight scales][token scales]
+  static constexpr uint32_t STAGE_MAX = W_STAGE + X_STAGE_MAX + 2 * SF_STAGE;
+  static constexpr uint32_t OFF_PART = STAGES * STAGE_MAX;  // 128 / 136 / 160 KB
+  static constexpr uint32_t OFF_EPI = OFF_PART + PART_MAX;
+  static constexpr uint32_t OFF_BAR = OFF_EPI + EPI_BYTES;
+  static constexpr uint32_t SMEM_BYTES = OFF_BAR + (2 * STAGES + 2) * 8 + 16 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(SF_STAGE % 512 == 0 && (2 * SF_STAGE) % 1024 == 0, "stages stay 1 KB aligned");
+};
 
 struct Params {
   const float *xs;
@@ -71,6 +94,7 @@ struct Params {
   int kps;           // K-blocks per split
   uint32_t idesc;
   uint32_t tmem_cols;
+  uint32_t sf_col;   // block-scaled: TMEM column of the weight scales (token scales follow)
   int pdl;
 };
 
@@ -86,15 +110,21 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
   }
 }
 
+template <int F>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                          const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+                          const __grid_constant__ CUtensorMap tmap_x,
+                          const __grid_constant__ CUtensorMap tmap_wsf,
+                          const __grid_constant__ CUtensorMap tmap_xsf, const Params p) {
+  using C = Cfg<F>;
+  constexpr uint32_t OFF_PART = C::OFF_PART, OFF_EPI = C::OFF_EPI, OFF_BAR = C::OFF_BAR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = ptx::smem_u32(smem);
   const uint32_t x_stage = static_cast<uint32_t>(p.mpad) * BK;
-  const uint32_t stage_bytes = W_STAGE + x_stage;  // multiple of 2 KB
+  const uint32_t sf_off = W_STAGE + x_stage;  // weight scale tiles; token tiles follow
+  const uint32_t stage_bytes = sf_off + 2 * C::SF_STAGE;  // multiple of 1 KB
   const uint32_t bar_full = sbase + OFF_BAR;
   const uint32_t bar_empty = bar_full + 8 * STAGES;
   const uint32_t bar_acc = bar_empty + 8 * STAGES;
@@ -114,6 +144,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&tmap_w);
     ptx::prefetch_tmap(&tmap_x);
+    if constexpr (C::BS) {
+      ptx::prefetch_tmap(&tmap_wsf);
+      ptx::prefetch_tmap(&tmap_xsf);
+    }
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
       ptx::mbar_init(bar_empty + 8 * s, 1);
@@ -123,15 +157,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     *abort = 0;
     ptx::fence_mbar_init();
     // The weights do not depend on the kernel this one may overlap (PDL): start streaming
-    // them now. The first stages' weight boxes land in shared memory (each stage's barrier
-    // is armed for its weight and token boxes; the token box follows after the dependency
-    // wait), the rest of this CTA's K-range is pulled into L2.
+    // them now. The first stages' weight boxes (and weight scale tiles) land in shared
+    // memory (each stage's barrier is armed for all its boxes; the token boxes follow after
+    // the dependency wait), the rest of this CTA's K-range is pulled into L2.
     const int pre = nkb < STAGES ? nkb : STAGES;
     for (int i = 0; i < pre; ++i) {
       const uint32_t fb = bar_full + 8 * i;
+      const uint32_t dst = sbase + static_cast<uint32_t>(i) * stage_bytes;
       ptx::mbar_arrive_expect_tx(fb, stage_bytes);
-      ptx::tma_load_2d(sbase + static_cast<uint32_t>(i) * stage_bytes, &tmap_w,
-                       (kb0 + i) * BK, tile * WN, fb);
+      ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
+      if constexpr (C::BS)
+        ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
     }
     for (int i = pre; i < nkb; ++i) ptx::tma_prefetch_2d(&tmap_w, (kb0 + i) * BK, tile * WN);
   }
@@ -163,8 +199,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           ptx::mbar_arrive_expect_tx(fb, stage_bytes);
           ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
-        }  // else: armed and the weight box issued before the dependency wait
+          if constexpr (C::BS)
+            ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
+        }  // else: armed and the weight boxes issued before the dependency wait
         ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, 0, fb);
+        if constexpr (C::BS)
+          ptx::tma_load_3d(dst + sf_off + C::SF_STAGE, &tmap_xsf, 0, (kb0 + i) * C::SF_TILES, 0,
+                           fb);
         ++issued;
       }
       for (int i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
@@ -189,10 +230,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t st = sbase + static_cast<uint32_t>(s) * stage_bytes;
         const uint64_t adesc = ptx::sw128_kmajor_desc(st);
         const uint64_t bdesc = ptx::sw128_kmajor_desc(st + W_STAGE);
+        const uint32_t sfa = tmem + p.sf_col;               // weight scales (scale A)
+        const uint32_t sfb = sfa + 4u * C::SF_TILES;        // token scales (scale B)
+        if constexpr (C::BS) {
+          // this K-block's scale tiles into TMEM, ahead of its MMAs in the same pipe
+#pragma unroll
+          for (int j = 0; j < C::SF_TILES; ++j) {
+            ptx::tmem_cp_32x128b_x4<1>(sfa + 4 * j, ptx::sf_block_desc(st + sf_off + 512 * j));
+            ptx::tmem_cp_32x128b_x4<1>(
+                sfb + 4 * j, ptx::sf_block_desc(st + sf_off + C::SF_STAGE + 512 * j));
+          }
+        }
 #pragma unroll
         for (int kk = 0; kk < BK / UMMA_K; ++kk) {
           const uint64_t koff = static_cast<uint64_t>((kk * UMMA_K) >> 4);
-          ptx::mma_f8f6f4(tmem, adesc + koff, bdesc + koff, p.idesc, (i | kk) != 0 ? 1u : 0u);
+          const uint32_t accumulate = (i | kk) != 0 ? 1u : 0u;
+          if constexpr (C::NV) {
+            // 64 elements = the four 16-element scales of word kk of each row
+            ptx::mma_nvf4<1>(tmem, adesc + koff, bdesc + koff, p.idesc, sfa + 4 * kk,
+                             sfb + 4 * kk, accumulate);
+          } else if constexpr (C::BS) {
+            // scale byte kk of each row's word: the kk-th 32-element block
+            const uint32_t sfid = static_cast<uint32_t>(kk) << 30;
+            ptx::mma_mxf8f6f4<1>(tmem, adesc + koff, bdesc + koff,
+                                 p.idesc | ptx::idesc_mx_e4m3(0, 0, kk), sfa | sfid,
+                                 sfb | sfid, accumulate);
+          } else {
+            ptx::mma_f8f6f4(tmem, adesc + koff, bdesc + koff, p.idesc, accumulate);
+          }
         }
         ptx::mma_commit(bar_empty + 8 * s);
       }
@@ -237,11 +302,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float *e_xs = reinterpret_cast<float *>(smem + OFF_EPI);  // [MAX_TOK]
   float *e_ws = e_xs + MAX_TOK;                              // [WN]: rows r0.. of the tile
   float *e_b = e_ws + WN;
-  for (int i = threadIdx.x; i < p.M; i += NUM_THREADS) e_xs[i] = __ldg(p.xs + i);
+  // block-scaled: the scales are inside the accumulator, out = fma(acc * 1, 1, bias)
+  for (int i = threadIdx.x; i < p.M; i += NUM_THREADS) e_xs[i] = C::BS ? 1.0f : __ldg(p.xs + i);
   for (int i = threadIdx.x; i < r1 - r0; i += NUM_THREADS) {
     const int n = tile * WN + r0 + i;
     const bool in = n < p.N;
-    e_ws[i] = in ? __ldg(p.ws + n) : 0.0f;
+    e_ws[i] = in ? (C::BS ? 1.0f : __ldg(p.ws + n)) : 0.0f;
     e_b[i] = in && p.bias_dtype != kNone ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
   }
 
@@ -294,18 +360,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
                      uint32_t box_inner, uint32_t box_outer, std::string *err);
+bool make_tmap_sf(CUtensorMap *map, const void *base, uint64_t rows, uint64_t ncb,
+                  uint32_t tiles_per_box, std::string *err);
 
-int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
-  using namespace small;
-  DeviceInfo dev;
-  if (!current_device_info(&dev)) return 5;
+namespace small {
+
+template <int F>
+int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
+  using C = Cfg<F>;
+  const char *name = C::NV ? "nvfp4_gemm: " : C::BS ? "mxfp8_gemm: " : "fp8_gemm: ";
   std::string err;
   const int mpad = static_cast<int>((a.M + 15) / 16 * 16);
-  CUtensorMap tw, tx;
-  if (!make_tmap_2d_u8(&tw, a.wq, a.K, a.N, BK, WN, &err) ||
-      !make_tmap_2d_u8(&tx, a.xq, a.K, a.M, BK, mpad, &err)) {
-    set_error("fp8_gemm: " + err);
+  // bytes of a row of codes (NV: two e2m1 codes per byte) and scale tiles per 128-row
+  // block (4 scales of 32 (MX) or 16 (NV) elements per tile)
+  const int64_t kbytes = C::NV ? a.K / 2 : a.K;
+  const int64_t ncb = C::NV ? (a.K / 16 + 3) / 4 : (a.K / 32 + 3) / 4;
+  CUtensorMap tw, tx, twsf, txsf;
+  if (!make_tmap_2d_u8(&tw, a.wq, kbytes, a.N, BK, WN, &err) ||
+      !make_tmap_2d_u8(&tx, a.xq, kbytes, a.M, BK, mpad, &err)) {
+    set_error(name + err);
     return 4;
+  }
+  if constexpr (C::BS) {
+    if (!make_tmap_sf(&twsf, a.wsf, a.N, ncb, C::SF_TILES, &err) ||
+        !make_tmap_sf(&txsf, a.xsf, a.M, ncb, C::SF_TILES, &err)) {
+      set_error(name + err);
+      return 4;
+    }
+  } else {  // unused by the kernel: any valid map
+    twsf = tw;
+    txsf = tw;
   }
   Params p;
   p.xs = a.xs;
@@ -319,20 +403,22 @@ int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   p.K = static_cast<int>(a.K);
   p.ldo = static_cast<int>(a.ldo > 0 ? a.ldo : a.N);
   p.mpad = mpad;
-  p.k_blocks = static_cast<int>((a.K + BK - 1) / BK);
+  p.k_blocks = static_cast<int>((kbytes + BK - 1) / BK);
   const int tiles = static_cast<int>((a.N + WN - 1) / WN);
 
   static std::once_flag once[64];
-  cudaError_t ce = cudaSuccess;
+  static cudaError_t setup_err[64];
   static int max_clusters[64][9];  // co-resident clusters per cluster size, per device
-  std::call_once(once[dev.device & 63], [&] {
-    ce = cudaFuncSetAttribute(fp8_gemm_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(SMEM_BYTES));
+  const int d = dev.device & 63;
+  std::call_once(once[d], [&] {
+    cudaError_t ce = cudaFuncSetAttribute(fp8_gemm_small_kernel<F>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(C::SMEM_BYTES));
     for (int c = 1; c <= 8 && ce == cudaSuccess; ++c) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3(c);
       q.blockDim = dim3(NUM_THREADS);
-      q.dynamicSmemBytes = SMEM_BYTES;
+      q.dynamicSmemBytes = C::SMEM_BYTES;
       cudaLaunchAttribute at[1];
       at[0].id = cudaLaunchAttributeClusterDimension;
       at[0].val.clusterDim.x = c;
@@ -341,35 +427,41 @@ int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
       q.attrs = at;
       q.numAttrs = 1;
       int n = 0;
-      ce = cudaOccupancyMaxActiveClusters(&n, fp8_gemm_small_kernel, &q);
-      max_clusters[dev.device & 63][c] = n;
+      ce = cudaOccupancyMaxActiveClusters(&n, fp8_gemm_small_kernel<F>, &q);
+      max_clusters[d][c] = n;
     }
+    setup_err[d] = ce;
   });
-  if (ce != cudaSuccess) {
-    set_error(std::string("fp8_gemm: small kernel setup: ") + cudaGetErrorString(ce));
+  if (setup_err[d] != cudaSuccess) {
+    set_error(std::string(name) + "small kernel setup: " + cudaGetErrorString(setup_err[d]));
     return 4;
   }
   // K-splits (= cluster size): the largest, at most 8, whose co-resident clusters hold
   // every weight tile in one wave; each split at least one K-block.
   int split = 1;
   for (int c = std::min(8, p.k_blocks); c >= 1; --c)
-    if (max_clusters[dev.device & 63][c] >= tiles) {
+    if (max_clusters[d][c] >= tiles) {
       split = c;
       break;
     }
   p.kps = (p.k_blocks + split - 1) / split;
   split = (p.k_blocks + p.kps - 1) / p.kps;
   p.split = split;
-  p.idesc = ptx::idesc_e4m3_f32(WN, mpad);
+  p.idesc = C::NV   ? ptx::idesc_nv_e2m1(WN, mpad)
+            : C::BS ? ptx::idesc_mx_e4m3(WN, mpad, 0)
+                    : ptx::idesc_e4m3_f32(WN, mpad);
+  // accumulator in columns [0, mpad), then the scale tiles: 4 columns per tile and operand
+  p.sf_col = static_cast<uint32_t>(mpad);
+  const uint32_t used = p.sf_col + 8u * C::SF_TILES;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(mpad)) cols <<= 1;
+  while (cols < used) cols <<= 1;
   p.tmem_cols = cols;
   p.pdl = pdl ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles * split);
   cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -384,12 +476,23 @@ int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  ce = cudaLaunchKernelEx(&cfg, fp8_gemm_small_kernel, tw, tx, p);
+  const cudaError_t ce =
+      cudaLaunchKernelEx(&cfg, fp8_gemm_small_kernel<F>, tw, tx, twsf, txsf, p);
   if (ce != cudaSuccess) {
-    set_error(std::string("fp8_gemm: small kernel launch failed: ") + cudaGetErrorString(ce));
+    set_error(std::string(name) + "small kernel launch failed: " + cudaGetErrorString(ce));
     return 4;
   }
   return 0;
+}
+
+}  // namespace small
+
+int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
+  DeviceInfo dev;
+  if (!current_device_info(&dev)) return 5;
+  if (a.nv) return small::launch<small::kFmtNV>(a, dev, stream, pdl);
+  if (a.mx) return small::launch<small::kFmtMX>(a, dev, stream, pdl);
+  return small::launch<small::kFmtE4M3>(a, dev, stream, pdl);
 }
 
 cudaError_t read_small_status(unsigned int *bits, bool clear) {
