@@ -811,20 +811,47 @@ __device__ __forceinline__ float2 mul2v(float2 a, float2 b) {
   return r;
 }
 
+// add / mul of two packed pairs of T with one rounding (IEEE, subnormals kept). For two
+// values of T they equal the fp32 operation followed by the rounding to T that a torch
+// elementwise op applies: a product of two 8- (11-) bit significands is exact in fp32, and
+// a sum is inexact in fp32 only when one operand is below 2^-16 (2^-13) of the other,
+// where the sum is too far from a midpoint of T's grid for the second rounding to differ.
 template <typename T>
 struct Rnd;
 template <>
 struct Rnd<__nv_bfloat16> {
+  static constexpr uint32_t kOne2 = 0x3F803F80u;  // (1, 1)
   __device__ __forceinline__ static uint32_t pack(float2 v) { return ptx::pack_bf16x2(v.x, v.y); }
   __device__ __forceinline__ static float2 unpack(uint32_t b) {
     return make_float2(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
   }
+  __device__ __forceinline__ static uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
 };
 template <>
 struct Rnd<__half> {
+  static constexpr uint32_t kOne2 = 0x3C003C00u;
   __device__ __forceinline__ static uint32_t pack(float2 v) { return ptx::pack_f16x2(v.x, v.y); }
   __device__ __forceinline__ static float2 unpack(uint32_t b) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&b));
+  }
+  __device__ __forceinline__ static uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
+  __device__ __forceinline__ static uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
   }
 };
 
@@ -883,9 +910,8 @@ __global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
   const float var = __fdiv_rn(warp_sum_xor(sq), kf);
   const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
   const int64_t boff = (row / rows_per_batch) * static_cast<int64_t>(K);
-  // y, two elements at a time
+  // y, two elements at a time: ln in fp32 and rounded, then m1, t and y as packed T ops
   const float2 rs2 = make_float2(rstd, rstd);
-  const float2 one2 = make_float2(1.0f, 1.0f);
   uint32_t mag = 0;  // packed max of |y| bit patterns (the amax of finite rows)
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {
@@ -899,10 +925,9 @@ __global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
       uint32_t w[4];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        const float2 ln = Rnd<T>::unpack(Rnd<T>::pack(mul2v(add2(Rnd<T>::unpack(xw[p]), nmean), rs2)));
-        const float2 m1 = Rnd<T>::unpack(Rnd<T>::pack(add2(one2, Rnd<T>::unpack(sw[p]))));
-        const float2 t = Rnd<T>::unpack(Rnd<T>::pack(mul2v(ln, m1)));
-        w[p] = Rnd<T>::pack(add2(t, Rnd<T>::unpack(hw[p])));
+        const uint32_t ln = Rnd<T>::pack(mul2v(add2(Rnd<T>::unpack(xw[p]), nmean), rs2));
+        const uint32_t m1 = Rnd<T>::add(Rnd<T>::kOne2, sw[p]);
+        w[p] = Rnd<T>::add(Rnd<T>::mul(ln, m1), hw[p]);
         mag = mag_max2(mag, w[p]);
       }
       v[i] = make_uint4(w[0], w[1], w[2], w[3]);
