@@ -39,10 +39,13 @@ def _unfused(x, shift, scale, eps=1e-6):
 
 @pytest.mark.parametrize("M,K,B,dtype", [(1, 8, 1, torch.bfloat16), (7, 96, 7, torch.bfloat16),
                                          (129, 1032, 3, torch.float16), (300, 264, 4, torch.bfloat16),
-                                         (256, 8192, 2, torch.float16), (4608, 3072, 2, torch.bfloat16)])
+                                         (256, 8192, 2, torch.float16), (4608, 3072, 2, torch.bfloat16),
+                                         (8192, 3072, 2, torch.bfloat16), (6003, 4104, 3, torch.bfloat16),
+                                         (3200, 8192, 4, torch.float16)])
 def test_fused_quantizer_vs_oracle(oracle, M, K, B, dtype):
     """Every CPL variant of the kernel (K/8 chunks over 32 lanes: 1 .. 32 per lane), ragged
-    chunk counts, one batch per row, fp16."""
+    chunk counts, one batch per row, fp16; inputs of 50 MB and more (several waves of
+    rows), ragged, and with the longest rows."""
     import fp8linear_b200 as f
 
     g = torch.Generator(device="cuda").manual_seed(M + K)
@@ -51,7 +54,7 @@ def test_fused_quantizer_vs_oracle(oracle, M, K, B, dtype):
     xq, xs = f.layernorm_modulate_quantize_fp8(x, shift, scale)
     torch.cuda.synchronize()
     dt = oracle.BF16 if dtype == torch.bfloat16 else oracle.F16
-    _, oq, osc = oracle.np_ln_modulate_quantize(bits16(x), bits16(shift), bits16(scale), 1e-6, dt)
+    _, oq, osc = oracle.c_ln_modulate_quantize(bits16(x), bits16(shift), bits16(scale), 1e-6, dt)
     assert np.array_equal(xs.cpu().numpy(), osc)
     assert np.array_equal(codes(xq), oq)
 
@@ -67,6 +70,28 @@ def test_fused_quantizer_edge_rows(oracle):
     x[5] *= 1e4
     x = x.to(torch.bfloat16).cuda()
     shift, scale = _mod(2, K, torch.bfloat16, seed=3)
+    import fp8linear_b200 as f
+
+    xq, xs = f.layernorm_modulate_quantize_fp8(x, shift, scale, 1e-5)
+    torch.cuda.synchronize()
+    _, oq, osc = oracle.c_ln_modulate_quantize(bits16(x), bits16(shift), bits16(scale), 1e-5)
+    assert np.array_equal(xs.cpu().numpy(), osc)
+    assert np.array_equal(codes(xq), oq)
+
+
+def test_fused_quantizer_edge_rows_large_input(oracle):
+    """The edge rows above at the head of a 50 MB input (rows in several waves)."""
+    K = 3072
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(8192, K, generator=g)
+    x[0] = 3.0
+    x[1, ::2] = float("inf")
+    x[2, 5] = float("nan")
+    x[3] = torch.linspace(-1e-30, 1e-30, K)
+    x[4] = torch.linspace(-3e38, 3e38, K)
+    x[5] *= 1e4
+    x = x.to(torch.bfloat16).cuda()
+    shift, scale = _mod(4, K, torch.bfloat16, seed=5)
     import fp8linear_b200 as f
 
     xq, xs = f.layernorm_modulate_quantize_fp8(x, shift, scale, 1e-5)
