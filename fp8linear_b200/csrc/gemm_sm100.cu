@@ -438,7 +438,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                              (acc ? C::ACC1_COL : 0u);
       const bool rows_live = row0 < p.M;  // a quarter wholly below M stores nothing
       // MX: the chunk the two accumulators share (accumulator 0's last, accumulator 1's
-      // first) is read first and released on bar_tovl before the others.
+      // first) is read first and released on bar_tovl as soon as it is in registers, so
+      // the next tile's first MMA waits for one TMEM load, not for a chunk's stores.
       bool ovl_done = !MX;
       auto release_overlap = [&]() {
         ptx::tc_fence_before();
@@ -467,6 +468,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ptx::tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * EPI_COLS + 32),
                                 *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         ptx::tmem_wait_ld();
+        if (MX && !ovl_done) release_overlap();  // chunk 0 is the shared one
         uint32_t packed[32];
         const float4 *w4 = reinterpret_cast<const float4 *>(par_ws + c * EPI_COLS);
         const float4 *b4 = reinterpret_cast<const float4 *>(par_b + c * EPI_COLS);
