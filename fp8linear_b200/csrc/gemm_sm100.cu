@@ -132,6 +132,7 @@ struct Params {
   int ncb;           // MX / NV: scale tiles per 128-row block (ceil(K / 128) / ceil(K / 64))
   int n_fastest;     // tile order
   int direct_store;  // rows not 16-byte multiples / unaligned: no TMA store
+  int wide_store;    // e4m3, N % 128 == 0, no peers: one store per two 64-column chunks
   void *out;         // output base (direct stores)
   int ldo;           // output row pitch (elements)
   int n_peers;       // peer copies of every output box (P2P stores)
@@ -172,7 +173,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_out,
                     const __grid_constant__ CUtensorMap tmap_sfa,
-                    const __grid_constant__ CUtensorMap tmap_sfb, const Params p) {
+                    const __grid_constant__ CUtensorMap tmap_sfb,
+                    const __grid_constant__ CUtensorMap tmap_out2, const Params p) {
   using C = Cfg<CG, F>;
   constexpr bool MX = C::MX;
   constexpr bool NV = C::NV;
@@ -493,7 +495,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         const uint32_t b = st_cnt & 1u;
-        if (!p.direct_store) {
+        if (F == kFmtE4M3 && p.wide_store) {
+          // Chunks 2k and 2k + 1 fill the two 4 KB halves of the warp's 8 KB box (each in
+          // the 32 x 64 swizzled layout below) and leave in one 3-D store: tmap_out2 views
+          // the output as [N / 64 chunks][M rows][64 columns], box {64, 32, 2}.
+          const int h = ci & 1;
+          if (h == 0) {
+            if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous box has been read
+            __syncwarp();
+          }
+          uint8_t *dst = buf0_ptr + h * EPI_BUF + lane * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4 *>(dst + ((q ^ (lane & 7)) << 4)) = make_uint4(
+                packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          if (h == 1) {
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              ptx::tma_store_3d(&tmap_out2, buf0, 0, row0, n0 / EPI_COLS - 1);
+              ptx::bulk_commit_group();
+            }
+          }
+        } else if (!p.direct_store) {
           // Reuse a staging buffer only after the store issued two boxes ago has read it.
           if (lane == 0) ptx::bulk_wait_group_read<1>();
           __syncwarp();
@@ -629,6 +653,29 @@ bool make_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
   return true;
 }
 
+// The output [M, ldo] (16-bit elements, N % 64 == 0) as [N / 64 chunks][M rows][64 columns]:
+// a box {64, 32, 2} is two adjacent 64-column chunks of 32 rows, 128-byte swizzled.
+bool make_tmap_out_wide(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                        uint64_t M, uint64_t N, uint64_t ldo, std::string *err) {
+  auto fn = encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is unavailable (driver entry point query failed)";
+    return false;
+  }
+  cuuint64_t dims[3] = {64, M, N / 64};
+  cuuint64_t strides[2] = {ldo * 2, 128};
+  cuuint32_t box[3] = {64, 32, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
 bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner,
                   uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                   CUtensorMapSwizzle swizzle, std::string *err) {
@@ -749,6 +796,18 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   p.ncb = static_cast<int>(ncb);
   p.n_fastest = a.M >= a.N ? 1 : 0;
   p.direct_store = direct ? 1 : 0;
+  CUtensorMap tout2 = tout;
+  p.wide_store = 0;
+  if (F == kFmtE4M3 && !direct && a.n_peers == 0 && a.N % 128 == 0) {
+    std::string werr;  // a view the driver does not take: 64-column boxes instead
+    if (make_tmap_out_wide(&tout2,
+                           a.out_dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           a.out, a.M, a.N, ldo, &werr))
+      p.wide_store = 1;
+    else
+      tout2 = tout;
+  }
   p.out = a.out;
   p.ldo = static_cast<int>(ldo);
   p.n_peers = a.n_peers;
@@ -796,7 +855,8 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
     tsfa = ta;
     tsfb = ta;
   }
-  cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, F>, ta, tb, tout, tsfa, tsfb, p);
+  cudaError_t ce =
+      cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, F>, ta, tb, tout, tsfa, tsfb, tout2, p);
   if (ce != cudaSuccess) {
     set_error(std::string("fp8_gemm: launch failed: ") + cudaGetErrorString(ce));
     return 4;

@@ -159,6 +159,16 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t src, int
       : "memory");
 }
 
+// 3-D tiled TMA store shared -> global; elements outside the tensor are clipped.
+__device__ __forceinline__ void tma_store_3d(const void *tmap, uint32_t src, int32_t x,
+                                             int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(x), "r"(y), "r"(z), "r"(src)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
