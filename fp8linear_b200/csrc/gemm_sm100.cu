@@ -132,7 +132,7 @@ struct Params {
   int ncb;           // MX / NV: scale tiles per 128-row block (ceil(K / 128) / ceil(K / 64))
   int n_fastest;     // tile order
   int direct_store;  // rows not 16-byte multiples / unaligned: no TMA store
-  int wide_store;    // e4m3, N % 128 == 0, no peers: one store per two 64-column chunks
+  int wide_store;    // N % 128 == 0, no peers: one store per two 64-column chunks
   void *out;         // output base (direct stores)
   int ldo;           // output row pitch (elements)
   int n_peers;       // peer copies of every output box (P2P stores)
@@ -457,7 +457,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll 1
       for (int ci = 0; ci < BN / EPI_COLS; ++ci) {
         if (MX && ci == 1 && !ovl_done) release_overlap();
-        const int c = (MX && acc == 0) ? (ci + BN / EPI_COLS - 1) % (BN / EPI_COLS) : ci;
+        // MX, accumulator 0: chunks in descending order, the shared (last) one first; the
+        // pairs stored together, {3, 2} and {1, 0}, stay adjacent
+        const int c = (MX && acc == 0) ? BN / EPI_COLS - 1 - ci : ci;
         const int n0 = nt * BN + c * EPI_COLS;
         if (!rows_live) break;   // warp-uniform
         if (n0 >= p.N) {
@@ -495,25 +497,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         const uint32_t b = st_cnt & 1u;
-        if (F == kFmtE4M3 && p.wide_store) {
+        if (p.wide_store) {
           // Chunks 2k and 2k + 1 fill the two 4 KB halves of the warp's 8 KB box (each in
-          // the 32 x 64 swizzled layout below) and leave in one 3-D store: tmap_out2 views
-          // the output as [N / 64 chunks][M rows][64 columns], box {64, 32, 2}.
-          const int h = ci & 1;
-          if (h == 0) {
+          // the 32 x 64 swizzled layout below) and leave in one 3-D store once both are
+          // staged: tmap_out2 views the output as [N / 64 chunks][M rows][64 columns],
+          // box {64, 32, 2}. N % 128 == 0, so a pair is wholly inside or outside N.
+          const bool first = (ci & 1) == 0;  // first of its pair in processing order
+          if (first) {
             if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous box has been read
             __syncwarp();
           }
-          uint8_t *dst = buf0_ptr + h * EPI_BUF + lane * 128;
+          uint8_t *dst = buf0_ptr + (c & 1) * EPI_BUF + lane * 128;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             *reinterpret_cast<uint4 *>(dst + ((q ^ (lane & 7)) << 4)) = make_uint4(
                 packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-          if (h == 1) {
+          if (!first) {
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              ptx::tma_store_3d(&tmap_out2, buf0, 0, row0, n0 / EPI_COLS - 1);
+              ptx::tma_store_3d(&tmap_out2, buf0, 0, row0, (n0 / EPI_COLS) & ~1);
               ptx::bulk_commit_group();
             }
           }
@@ -798,7 +801,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   p.direct_store = direct ? 1 : 0;
   CUtensorMap tout2 = tout;
   p.wide_store = 0;
-  if (F == kFmtE4M3 && !direct && a.n_peers == 0 && a.N % 128 == 0) {
+  if (!direct && a.n_peers == 0 && a.N % 128 == 0) {
     std::string werr;  // a view the driver does not take: 64-column boxes instead
     if (make_tmap_out_wide(&tout2,
                            a.out_dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
