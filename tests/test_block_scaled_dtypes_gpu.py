@@ -28,7 +28,8 @@ def _case(M, N, K, seed, bias_dtype):
 
 @pytest.mark.parametrize("fmt", ["mx", "nv"])
 @pytest.mark.parametrize("M,N,K,bias_dtype", [(64, 264, 256, torch.float32), (300, 520, 512, None),
-                                              (129, 256, 1024, torch.float32)])
+                                              (129, 256, 1024, torch.float32),
+                                              (333, 384, 512, torch.bfloat16), (300, 640, 1024, None)])
 def test_block_scaled_fp16(oracle, capi, fmt, M, N, K, bias_dtype):
     import fp8linear_b200 as f
 

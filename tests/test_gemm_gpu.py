@@ -52,7 +52,8 @@ def _oracle_out(oracle, xq, xs, wq, ws, b):
     "M,N,K",
     [(1, 8, 16), (7, 24, 48), (128, 256, 128), (129, 264, 144), (300, 520, 1040),
      (256, 1024, 1024), (1000, 3072, 3072), (64, 9216, 3072), (513, 776, 4096),
-     (255, 512, 12288), (3, 1, 16), (64, 44, 1024), (200, 100, 512), (257, 1003, 256)],
+     (255, 512, 12288), (3, 1, 16), (64, 44, 1024), (200, 100, 512), (257, 1003, 256),
+     (333, 384, 1024), (1000, 640, 512)],
 )
 def test_gemm_shapes_vs_oracle(M, N, K, oracle):
     from fp8linear_b200 import ops
@@ -63,6 +64,20 @@ def test_gemm_shapes_vs_oracle(M, N, K, oracle):
     ref = _oracle_out(oracle, xq, xs, wq, ws, b)
     err = max_rel(out.cpu(), torch.from_numpy(ref))
     assert err <= OUT_TOL, err
+
+
+@pytest.mark.parametrize("M,N", [(333, 384), (200, 1152)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+def test_gemm_paired_stores_edges(M, N, out_dtype, capi, oracle):
+    """Output widths that are multiples of 128 but not of the 256-column tile (the last
+    tile's second chunk pair lies past N and is not stored), rows not a multiple of 32,
+    both output types: the paired 3-D stores write exactly the [M, N] block."""
+    xq, xs, wq, ws, b = _operands(M, N, 512, seed=M + N)
+    out = capi.fp8_gemm(xq, xs, wq, ws, b, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert out.dtype == out_dtype and out.shape == (M, N)
+    ref = _oracle_out(oracle, xq, xs, wq, ws, b)
+    assert max_rel(out.float().cpu(), torch.from_numpy(ref)) <= OUT_TOL
 
 
 @pytest.mark.parametrize("bias_dtype", [None, torch.bfloat16, torch.float16, torch.float32])
