@@ -1,7 +1,9 @@
 """Fused column-parallel linear (fp8lin_fp8_linear_allgather) on one GPU: extra local
 buffers stand in for the peers' output buffers, so the epilogue's peer-store path is
 checked without a second GPU. Every copy of this rank's column block must equal the
-plain fused linear on the shard, and no column outside the block may change."""
+plain fused linear on the shard, and no column outside the block may change. With a
+single buffer (no peers) the epilogue's paired stores write a column block of a wider
+row pitch (ldo > N)."""
 from __future__ import annotations
 
 import pytest
@@ -13,10 +15,11 @@ from tests.helpers import require_sm100
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("single", [False, True])
 @pytest.mark.parametrize("M,N_total,K,world,rank",
                          [(300, 1024, 512, 2, 1), (4608, 3072, 3072, 4, 2), (129, 768, 256, 3, 0),
                           (65, 64, 128, 8, 7)])
-def test_allgather_epilogue_writes_every_copy(M, N_total, K, world, rank, capi):
+def test_allgather_epilogue_writes_every_copy(M, N_total, K, world, rank, single, capi):
     require_sm100()
     import fp8linear_b200 as f
 
@@ -27,7 +30,7 @@ def test_allgather_epilogue_writes_every_copy(M, N_total, K, world, rank, capi):
     wq, ws = f.quantize_weight(w)
     s, e = column_range(N_total, world, rank)
     ref = f.fp8_linear(x, wq[s:e].contiguous(), ws[s:e].contiguous(), b[s:e].contiguous())
-    n_copies = min(world, 3)
+    n_copies = 1 if single else min(world, 3)
     sentinel = torch.tensor(-7.0, dtype=torch.bfloat16)
     bufs = [torch.full((M, N_total), float(sentinel), dtype=torch.bfloat16, device="cuda")
             for _ in range(n_copies)]
