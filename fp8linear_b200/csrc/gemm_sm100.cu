@@ -897,19 +897,27 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
     set_error("fp8_gemm: dimensions must fit in int32 and at most 7 peers");
     return 2;
   }
-  // MXFP8 / NVFP4: the few-token kernel for M <= 128, CTA pairs otherwise.
+  // MXFP8 / NVFP4: the few-token kernel for M <= 128, and up to 256 where it gets a
+  // K-split; CTA pairs otherwise.
   if (a.mx) {
     if (a.n_peers != 0) {
       set_error("block-scaled gemm: peer outputs are not supported");
       return 2;
     }
-    if (a.M <= gemm::BM) return launch_gemm_small(a, stream, pdl);
+    if (a.M <= 2 * gemm::BM) {
+      const int rc = launch_gemm_small(a, stream, pdl);
+      if (rc != kSmallDeclined) return rc;
+    }
     if (a.nv) return gemm::launch_shape<2, gemm::kFmtNV>(a, dev, stream, pdl);
     return gemm::launch_shape<2, gemm::kFmtMX>(a, dev, stream, pdl);
   }
-  // Few tokens: stream the weights with swap-AB split-K tiles. Otherwise CTA pairs with
-  // 256-row tiles (or single CTAs with 128-row tiles for peer outputs at M <= 128).
-  if (a.M <= gemm::BM && a.n_peers == 0) return launch_gemm_small(a, stream, pdl);
+  // Few tokens: stream the weights with swap-AB split-K tiles (M <= 128; up to 256 where
+  // the kernel gets a K-split). Otherwise CTA pairs with 256-row tiles (or single CTAs
+  // with 128-row tiles for peer outputs at M <= 128).
+  if (a.M <= 2 * gemm::BM && a.n_peers == 0) {
+    const int rc = launch_gemm_small(a, stream, pdl);
+    if (rc != kSmallDeclined) return rc;
+  }
   if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtE4M3>(a, dev, stream, pdl);
   return gemm::launch_shape<2, gemm::kFmtE4M3>(a, dev, stream, pdl);
 }

@@ -1,5 +1,7 @@
 // gemm_small_sm100.cu -- the FP8 GEMM + fused dequant/bias epilogue for few tokens
-// (M <= 128), where the work is streaming the weight matrix once.
+// (M <= 128, and M <= 256 where it gets a K-split), where the work is streaming the weight
+// matrix once. Tokens go in blocks of 128 (grid y); each (weight tile, token block) pair
+// is one cluster.
 //
 // Same result as fp8_gemm_kernel (out[m,n] = fma(acc * x_scale[m], w_scale[n], bias[n]),
 // acc = e4m3 dot products accumulated in fp32), organised for a weight-bandwidth-bound
@@ -137,6 +139,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = ptx::cluster_ctarank();  // K-split index
   const int tile = blockIdx.x / p.split;         // 128-row weight tile
+  const int mb = blockIdx.y;                     // block of MAX_TOK tokens
+  const int tok0 = mb * MAX_TOK;
+  const int mrows = min(MAX_TOK, p.M - tok0);    // tokens of this block
   const int kb0 = static_cast<int>(rank) * p.kps;
   const int kb1 = min(p.k_blocks, kb0 + p.kps);
   const int nkb = kb1 - kb0;  // >= 1 (host guarantees)
@@ -202,9 +207,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if constexpr (C::BS)
             ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
         }  // else: armed and the weight boxes issued before the dependency wait
-        ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, 0, fb);
+        ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, tok0, fb);
         if constexpr (C::BS)
-          ptx::tma_load_3d(dst + sf_off + C::SF_STAGE, &tmap_xsf, 0, (kb0 + i) * C::SF_TILES, 0,
+          ptx::tma_load_3d(dst + sf_off + C::SF_STAGE, &tmap_xsf, 0, (kb0 + i) * C::SF_TILES, mb,
                            fb);
         ++issued;
       }
@@ -303,7 +308,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float *e_ws = e_xs + MAX_TOK;                              // [WN]: rows r0.. of the tile
   float *e_b = e_ws + WN;
   // block-scaled: the scales are inside the accumulator, out = fma(acc * 1, 1, bias)
-  for (int i = threadIdx.x; i < p.M; i += NUM_THREADS) e_xs[i] = C::BS ? 1.0f : __ldg(p.xs + i);
+  for (int i = threadIdx.x; i < mrows; i += NUM_THREADS)
+    e_xs[i] = C::BS ? 1.0f : __ldg(p.xs + tok0 + i);
   for (int i = threadIdx.x; i < r1 - r0; i += NUM_THREADS) {
     const int n = tile * WN + r0 + i;
     const bool in = n < p.N;
@@ -318,7 +324,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // Each task is 4 consecutive rows of one token: the loads from all ranks' shared memory
   // are issued together, then summed in rank order.
   const uint32_t part_base = ptx::smem_u32(part);
-  for (int idx = threadIdx.x; idx < p.M * quads; idx += NUM_THREADS) {
+  for (int idx = threadIdx.x; idx < mrows * quads; idx += NUM_THREADS) {
     const int m = idx / quads;
     const int nl = r0 + 4 * (idx - m * quads);
     const uint32_t off = static_cast<uint32_t>(m * WN + nl) * 4u;
@@ -341,7 +347,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int n = tile * WN + nl + e;
       if (n >= p.N) break;
       const float val = fmaf(acc[e] * xs, e_ws[nl - r0 + e], e_b[nl - r0 + e]);
-      const int64_t o = static_cast<int64_t>(m) * p.ldo + n;
+      const int64_t o = static_cast<int64_t>(tok0 + m) * p.ldo + n;
       if (p.out_dtype == kF16)
         reinterpret_cast<__half *>(p.out)[o] = __float2half_rn(val);
       else
@@ -370,7 +376,9 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
   using C = Cfg<F>;
   const char *name = C::NV ? "nvfp4_gemm: " : C::BS ? "mxfp8_gemm: " : "fp8_gemm: ";
   std::string err;
-  const int mpad = static_cast<int>((a.M + 15) / 16 * 16);
+  // tokens per block padded to a multiple of 16 (MMA N); blocks of MAX_TOK tokens
+  const int mpad = a.M > MAX_TOK ? MAX_TOK : static_cast<int>((a.M + 15) / 16 * 16);
+  const int nblk = static_cast<int>((a.M + MAX_TOK - 1) / MAX_TOK);
   // bytes of a row of codes (NV: two e2m1 codes per byte) and scale tiles per 128-row
   // block (4 scales of 32 (MX) or 16 (NV) elements per tile)
   const int64_t kbytes = C::NV ? a.K / 2 : a.K;
@@ -437,13 +445,15 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
     return 4;
   }
   // K-splits (= cluster size): the largest, at most 8, whose co-resident clusters hold
-  // every weight tile in one wave; each split at least one K-block.
+  // every (weight tile, token block) pair in one wave; each split at least one K-block.
   int split = 1;
   for (int c = std::min(8, p.k_blocks); c >= 1; --c)
-    if (max_clusters[d][c] >= tiles) {
+    if (max_clusters[d][c] >= tiles * nblk) {
       split = c;
       break;
     }
+  // Above one token block, a launch without a K-split loses to the CTA-pair kernel.
+  if (nblk > 1 && split < 2) return kSmallDeclined;
   p.kps = (p.k_blocks + split - 1) / split;
   split = (p.k_blocks + p.kps - 1) / p.kps;
   p.split = split;
@@ -459,7 +469,7 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
   p.pdl = pdl ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles * split);
+  cfg.gridDim = dim3(tiles * split, nblk);
   cfg.blockDim = dim3(NUM_THREADS);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;

@@ -103,7 +103,11 @@ cudaError_t read_gemm_status(unsigned int *bits, bool clear);
 cudaError_t launch_watchdog_selftest(unsigned int limit_us, unsigned int *status,
                                      cudaStream_t stream);
 
-// ---- gemm_small_sm100.cu (M <= 128: swap-AB, split-K over a cluster)
+// ---- gemm_small_sm100.cu (M <= 256: swap-AB, split-K over a cluster)
+// Returns an fp8lin_status code, or kSmallDeclined without launching when M > 128 and
+// the (weight tile, token block) clusters would get no K-split (split 1: every CTA
+// streams all of K alone, slower than the CTA-pair kernel); the caller then launches that.
+constexpr int kSmallDeclined = -1;
 int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl);
 cudaError_t read_small_status(unsigned int *bits, bool clear);
 // 2-D uint8 tensor map with 128-byte swizzle (shared by both GEMM shapes).
