@@ -1,5 +1,6 @@
-"""MXFP8 and NVFP4 GEMMs for few tokens (M <= 128) on the GPU: the split-K swap-AB kernel
-with the weight's scale tiles as the MMA's scale A and the tokens' as its scale B. Exact
+"""MXFP8 and NVFP4 GEMMs for few tokens (M <= 128, and two 128-token blocks up to 256) on
+the GPU: the split-K swap-AB kernel with the weight's scale tiles as the MMA's scale A and
+the tokens' as its scale B. Exact
 against a float64 product when every scale is a power of two and every sum is exact in
 fp32 (so a scale tile or TMEM column out of place changes the bits); within OUT_TOL of the
 oracle (restating csrc/fp8_gemm.cu:233-333 and 352-445) on normal data; the fused linear
@@ -41,12 +42,13 @@ def _pow2_blocks(rows, K, block, g):
 
 
 @pytest.mark.parametrize("fmt", ["mx", "nv"])
-@pytest.mark.parametrize("M", [1, 16, 37, 128, 256])
+@pytest.mark.parametrize("M", [1, 16, 37, 128, 200, 256, 257])
 def test_exact_power_of_two_scales(fmt, M):
     """Per-row, per-block scales 1 or 2 on both operands: products and partial sums are
     integers of a few thousand, exact in fp32 in any summation order, so the output is the
     exact product rounded once to bf16, and a scale applied to the wrong row or block
-    changes it. M = 256 checks the CTA-pair kernel the same way."""
+    changes it. M = 200 and 256 use two token blocks (the second block's rows and scale
+    tiles from row 128); M = 257 checks the CTA-pair kernel the same way."""
     qx, qw, gemm, _ = _ops(fmt)
     N, K = 384, 1024
     block = 32 if fmt == "mx" else 16
@@ -95,7 +97,7 @@ def test_vs_oracle(oracle, fmt, M, N, K):
 
 
 @pytest.mark.parametrize("fmt", ["mx", "nv"])
-@pytest.mark.parametrize("M", [1, 16, 100, 128])
+@pytest.mark.parametrize("M", [1, 16, 100, 128, 200, 256])
 def test_linear_equals_quantize_then_gemm(fmt, M):
     """The fused linear (GEMM launched as the quantizer's programmatic dependent, weight
     tiles requested before the dependency wait) gives the two-step path's bits."""
