@@ -1,7 +1,9 @@
 """Fused column-parallel linear (fp8lin_fp8_linear_allgather) on one GPU: extra local
 buffers stand in for the peers' output buffers, so the epilogue's peer-store path is
-checked without a second GPU. Every copy of this rank's column block must equal the
-plain fused linear on the shard, and no column outside the block may change. With a
+checked without a second GPU. Every copy of this rank's column block must hold the same
+bits, within OUT_TOL of the plain fused linear on the shard (which, for M <= 512, may run
+the split-K few-token kernel, whose fp32 summation order differs from the CTA-pair
+kernel's), and no column outside the block may change. With a
 single buffer (no peers) the epilogue's paired stores write a column block of a wider
 row pitch (ldo > N)."""
 from __future__ import annotations
@@ -10,7 +12,7 @@ import pytest
 import torch
 
 from fp8linear_b200.sharding import column_range
-from tests.helpers import require_sm100
+from tests.helpers import OUT_TOL, max_rel, require_sm100
 
 pytestmark = pytest.mark.gpu
 
@@ -38,8 +40,10 @@ def test_allgather_epilogue_writes_every_copy(M, N_total, K, world, rank, single
     capi.fp8_linear_allgather(x, wq[s:e].contiguous(), ws[s:e].contiguous(),
                               b[s:e].contiguous(), ptrs, ldo=N_total)
     torch.cuda.synchronize()
+    first = bufs[0][:, s:e]
+    assert max_rel(first.float().cpu(), ref.float().cpu()) <= OUT_TOL
     for t in bufs:
-        assert torch.equal(t[:, s:e], ref)
+        assert torch.equal(t[:, s:e], first)
         outside = torch.cat([t[:, :s].flatten(), t[:, e:].flatten()])
         assert (outside == sentinel).all()
     assert capi.device_status() == 0

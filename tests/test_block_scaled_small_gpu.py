@@ -42,13 +42,13 @@ def _pow2_blocks(rows, K, block, g):
 
 
 @pytest.mark.parametrize("fmt", ["mx", "nv"])
-@pytest.mark.parametrize("M", [1, 16, 37, 128, 200, 256, 257])
+@pytest.mark.parametrize("M", [1, 16, 37, 128, 200, 256, 384, 500, 513])
 def test_exact_power_of_two_scales(fmt, M):
     """Per-row, per-block scales 1 or 2 on both operands: products and partial sums are
     integers of a few thousand, exact in fp32 in any summation order, so the output is the
     exact product rounded once to bf16, and a scale applied to the wrong row or block
     changes it. M = 200 and 256 use two token blocks (the second block's rows and scale
-    tiles from row 128); M = 257 checks the CTA-pair kernel the same way."""
+    tiles from row 128); M = 384, 500 and 513 check the CTA-pair kernel the same way."""
     qx, qw, gemm, _ = _ops(fmt)
     N, K = 384, 1024
     block = 32 if fmt == "mx" else 16
@@ -97,7 +97,7 @@ def test_vs_oracle(oracle, fmt, M, N, K):
 
 
 @pytest.mark.parametrize("fmt", ["mx", "nv"])
-@pytest.mark.parametrize("M", [1, 16, 100, 128, 200, 256])
+@pytest.mark.parametrize("M", [1, 16, 100, 128, 200, 256, 384])
 def test_linear_equals_quantize_then_gemm(fmt, M):
     """The fused linear (GEMM launched as the quantizer's programmatic dependent, weight
     tiles requested before the dependency wait) gives the two-step path's bits."""

@@ -53,7 +53,8 @@ def _oracle_out(oracle, xq, xs, wq, ws, b):
     [(1, 8, 16), (7, 24, 48), (128, 256, 128), (129, 264, 144), (300, 520, 1040),
      (256, 1024, 1024), (1000, 3072, 3072), (64, 9216, 3072), (513, 776, 4096),
      (255, 512, 12288), (3, 1, 16), (64, 44, 1024), (200, 100, 512), (257, 1003, 256),
-     (333, 384, 1024), (1000, 640, 512), (192, 3072, 3072), (256, 9216, 3072)],
+     (333, 384, 1024), (1000, 640, 512), (192, 3072, 3072), (256, 9216, 3072),
+     (384, 1024, 3072), (500, 2048, 2048)],
 )
 def test_gemm_shapes_vs_oracle(M, N, K, oracle):
     from fp8linear_b200 import ops
