@@ -55,6 +55,34 @@ L2_FALLBACK = 126 << 20
 # ----------------------------------------------------------------------------- plumbing
 
 
+def _workloads():
+    """fp8linear_b200/workloads.py (the seeded input generators) loaded as a module of
+    its own, without importing the package: the package's import maps the native
+    binding, which the reference arm must not load."""
+    import importlib.util
+
+    name = "fp8linear_b200_bench_workloads"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(
+            name, ROOT / "fp8linear_b200" / "workloads.py")
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
+DATA = "synthetic (seeded FLUX-shaped tensors; FLUX.1-dev weights unavailable offline)"
+
+
+def bench_config(wl, world: int) -> dict:
+    """The ``config`` of the driver's line, identical in both arms."""
+    return {"workload": wl.name, "M_per_gpu": wl.M, "K": wl.K, "N": wl.N,
+            "global_tokens": wl.M * world, "x": "bf16", "out": "bf16",
+            "parallelism": f"M-shard x{world}, weights replicated, no collective",
+            "l2": "inputs larger than L2: steps rotate over operand sets (x, weight, "
+                  "output) so that 3x the L2 is touched between two uses of a set"}
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -199,8 +227,9 @@ def operand_sets(wl, n_sets: int, x_seed0: int = 0, quantize_x: bool = True, fmt
     "fp8": per-token / per-channel scales; "mx": MXFP8 block scales; "nv": NVFP4;
     "modulated": per-channel weights plus the AdaLN shift / scale [2, K] of a 2-image batch."""
     import fp8linear_b200 as f
-    from fp8linear_b200.workloads import make_weight, make_x
 
+    W = _workloads()
+    make_weight, make_x = W.make_weight, W.make_x
     qw = {"fp8": f.quantize_weight, "mx": f.quantize_weight_mxfp8,
           "nv": f.quantize_weight_nvfp4, "modulated": f.quantize_weight}[fmt]
     qx = {"fp8": f.quantize_fp8, "mx": f.quantize_mxfp8, "nv": f.quantize_nvfp4,
@@ -281,12 +310,15 @@ def cpu_reference_runner(wl, rows: int, threads: int | None = None):
     """The reference path on the CPU (oracle port) for ``rows`` token rows of ``wl``.
 
     The weight is quantized once (offline, as the reference's quantize_weight) and kept
-    decoded to fp32; each call quantizes x per token, decodes the codes, runs the fp32
-    matmul and applies (acc * xs) * ws + bias.
+    decoded to fp32; each call quantizes x per token (the oracle's multi-threaded torch
+    twin), decodes the codes, runs the fp32 matmul and applies (acc * xs) * ws + bias in
+    place (the same roundings as the expression).
     """
     import numpy as np
     from oracle import oracle as O
-    from fp8linear_b200.workloads import make_weight, make_x
+
+    W = _workloads()
+    make_weight, make_x = W.make_weight, W.make_x
 
     if threads:
         torch.set_num_threads(threads)
@@ -298,13 +330,12 @@ def cpu_reference_runner(wl, rows: int, threads: int | None = None):
     wf = lut[torch.from_numpy(wq).long()]
     wsv = torch.from_numpy(ws)
     bias = b.float()
-    x16 = x.contiguous().view(torch.int16).numpy().view(np.uint16)
+    x = x.contiguous()
 
     def step():
-        xq, xs = O.np_quantize_rows(x16, O.BF16)
-        a = lut[torch.from_numpy(xq).long()]
-        acc = a @ wf.T
-        return (acc * torch.from_numpy(xs)[:, None]) * wsv[None, :] + bias[None, :]
+        xq, xs = O.torch_quantize_rows(x)
+        acc = xq.float() @ wf.T
+        return acc.mul_(xs[:, None]).mul_(wsv[None, :]).add_(bias[None, :])
 
     return step
 
@@ -330,13 +361,12 @@ def run_gpu(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     import fp8linear_b200 as f
     from fp8linear_b200.capi import CApi
-    from fp8linear_b200.workloads import WORKLOADS
 
-    wl = WORKLOADS[args.workload]
+    wl = _workloads().WORKLOADS[args.workload]
     M, K, N = wl.M, wl.K, wl.N
     per_set = per_set_bytes(wl)
     n_sets = set_count(per_set, dev)
@@ -449,13 +479,10 @@ def run_gpu(args):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "e4m3",
-            "data": "synthetic (seeded FLUX-shaped tensors; FLUX.1-dev weights unavailable offline)",
-            "config": {"workload": wl.name, "M_per_gpu": M, "K": K, "N": N,
-                       "global_tokens": M * world, "x": "bf16", "out": "bf16",
-                       "parallelism": f"M-shard x{world}, weights replicated, no collective",
-                       "l2": f"inputs larger than L2: {n_sets} rotating operand sets of "
-                             f"{per_set / 1e6:.0f} MB (x, weight, output); steps back to back "
-                             f"in one CUDA graph"},
+            "data": DATA,
+            "config": bench_config(wl, world),
+            "timing": f"{args.steps} steps back to back in one CUDA graph over {n_sets} "
+                      f"rotating operand sets of {per_set / 1e6:.0f} MB",
             "roofline": {"bound": "tensor", "kernel": "fp8_gemm_kernel",
                          "achieved": round(gemm_tflops, 1), "peak": round(fp8_peak, 1),
                          "unit": "TFLOP/s", "frac": round(gemm_tflops / fp8_peak, 4),
@@ -477,10 +504,220 @@ def run_gpu(args):
             "clocks": clk,
             "watchdog_status": status,
         }
+    # ---- north-star sharded configurations, measured after the headline (not part of
+    # its timed region): config 4 strong-scaled over the ranks, config 5 column-parallel
+    if not args.no_extras:
+        sets = x = wq = ws = b = work = None  # free the headline's operands
+        torch.cuda.empty_cache()
+        extra_clocks = ClockSampler(local).start()
+        try:
+            cfg4 = mshard_cfg4(args, world, rank, dev, barrier)
+        except Exception as e:  # the headline line is still printed
+            cfg4 = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+        torch.cuda.empty_cache()
+        try:
+            cfg5 = nshard_cfg5(args, world, rank, dev, barrier)
+        except Exception as e:
+            cfg5 = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+        torch.cuda.empty_cache()
+        eclk = extra_clocks.stop()
+        if rank == 0:
+            line["mshard_cfg4"] = cfg4
+            line["nshard_cfg5"] = cfg5
+            line["extras_clocks"] = eclk
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _max_over_ranks(vals, world, dev):
+    """Element-wise max over ranks of a list of floats (device times)."""
+    if world == 1:
+        return list(vals)
+    import torch.distributed as dist
+
+    t = torch.tensor(list(vals), device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def _graph_ms(call, sets, steps, stream, barrier) -> float:
+    """Device ms of ``steps`` calls back to back in one CUDA graph over ``sets``."""
+    g = graph_launches(call, sets, steps, keep=len(sets))
+    ms = time_graph(g, stream, barrier)
+    del g
+    return ms
+
+
+def mshard_cfg4(args, world, rank, dev, barrier) -> dict:
+    """Config 4: the FLUX single-stream block linears at batch 4 (linear1 18432 x 3072 ->
+    21504, linear2 18432 x 15360 -> 3072) with the GLOBAL 18432 token rows split over the
+    ranks (strong scaling), weights replicated, no collective. Each rank times its row
+    block (steps back to back over rotating operand sets, as the headline); the job time
+    is the max over ranks. Rank 0 also times all 18432 rows alone on its GPU, the
+    one-GPU figure the efficiency is taken against (t1 / (N x tN))."""
+    import dataclasses
+
+    import fp8linear_b200 as f
+    from fp8linear_b200.sharding import row_range
+
+    W = _workloads()
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for name in ("flux_linear1", "flux_linear2"):
+        wl = W.WORKLOADS[name]
+        s0, e0 = row_range(wl.M, world, rank)
+        wl_r = dataclasses.replace(wl, M=e0 - s0)
+
+        def step(st):
+            return f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"])
+
+        sets = operand_sets(wl_r, set_count(per_set_bytes(wl_r), dev), x_seed0=1000 * rank,
+                            quantize_x=False)
+        for i in range(args.warmup):
+            step(sets[i % len(sets)])
+        barrier()
+        t_n = _max_over_ranks([_graph_ms(step, sets, args.steps, stream, barrier)], world,
+                              dev)[0] / args.steps
+        del sets
+        torch.cuda.empty_cache()
+        t_1 = t_n
+        if world > 1:
+            t1 = torch.zeros(1, device=dev, dtype=torch.float64)
+            if rank == 0:
+                sets = operand_sets(wl, set_count(per_set_bytes(wl), dev), quantize_x=False)
+                for i in range(args.warmup):
+                    step(sets[i % len(sets)])
+                torch.cuda.synchronize(dev)
+                t1[0] = _graph_ms(step, sets, args.steps, stream,
+                                  lambda: torch.cuda.synchronize(dev)) / args.steps
+                del sets
+                torch.cuda.empty_cache()
+            import torch.distributed as dist
+
+            dist.broadcast(t1, 0)
+            t_1 = float(t1.item())
+        tf_n = wl.flops / (t_n * 1e-3) / 1e12
+        tf_1 = wl.flops / (t_1 * 1e-3) / 1e12
+        out[name.replace("flux_", "")] = {
+            "global_M": wl.M, "K": wl.K, "N": wl.N, "rows_per_gpu_max": -(-wl.M // world),
+            "value": round(tf_n, 1), "unit": "TFLOP/s", "ms_per_step": round(t_n, 4),
+            "one_gpu_tflops": round(tf_1, 1), "one_gpu_ms": round(t_1, 4),
+            "speedup": round(t_1 / t_n, 3), "efficiency": round(t_1 / (world * t_n), 4)}
+    out["scaling"] = "strong"
+    out["how"] = ("fp8_linear (quantizer + GEMM) on each rank's block of the global 18432 "
+                  f"rows, {args.steps} steps back to back in one CUDA graph over rotating "
+                  "operand sets, max over ranks; one_gpu: all rows on rank 0's GPU alone")
+    return out
+
+
+def nshard_cfg5(args, world, rank, dev, barrier) -> dict:
+    """Config 5 at M = 65536, K = N = 3072: column-parallel over the ranks (each rank
+    holds N/world output channels and quantizes the full, replicated x), the output
+    gathered to every rank as row-major [M, N] two ways: (a) the rank's fused linear, then
+    NCCL all_gather_into_tensor + one interleave copy; (b) the all-gather fused into the
+    GEMM epilogue (16-byte P2P stores into every rank's peer buffer over NVLink, then a
+    one-element all-reduce). Both results are compared bit for bit with the unsharded
+    one-GPU result computed on every rank. Steps run eagerly (x and the output are
+    403 MB each, beyond L2), each bracketed by CUDA events; max over ranks."""
+    import fp8linear_b200 as f
+    from fp8linear_b200 import sharding as S
+    from fp8linear_b200.capi import CApi
+
+    W = _workloads()
+    wl = W.WORKLOADS["sweep_M65536"]
+    stream = torch.cuda.current_stream(dev)
+    x = W.make_x(wl, gen_device="cuda")
+    w, b = W.make_weight(wl, gen_device="cuda")
+    wq, ws = f.quantize_weight(w)
+    del w
+    full = f.fp8_linear(x, wq, ws, b)
+
+    def timed(fn, n):
+        """Per-step device ms (total, to the mid event) of ``n`` eager steps."""
+        for _ in range(args.warmup):
+            fn(None)
+        barrier()
+        ev = []
+        for _ in range(n):
+            a, m, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            a.record(stream)
+            fn(m)
+            c.record(stream)
+            ev.append((a, m, c))
+        barrier()
+        tot = sum(a.elapsed_time(c) for a, m, c in ev) / n
+        mid = sum(a.elapsed_time(m) for a, m, c in ev) / n
+        return tot, mid
+
+    def unsharded(mark):
+        o = f.fp8_linear(x, wq, ws, b)
+        if mark is not None:
+            mark.record(stream)
+        return o
+
+    t_full, _ = timed(unsharded, args.steps)
+    t_full = _max_over_ranks([t_full], world, dev)[0]
+    res = {"M": wl.M, "K": wl.K, "N": wl.N, "one_gpu_ms": round(t_full, 4),
+           "one_gpu_tflops": round(wl.flops / (t_full * 1e-3) / 1e12, 1)}
+    if world == 1:
+        res["note"] = "one GPU: the unsharded linear only"
+        return res
+    wqs, wss, bs = S.shard_columns(wq, ws, b, world, rank)
+    n_loc = wl.N // world
+    peer_bytes = (world - 1) * wl.M * n_loc * 2  # bytes each rank sends (and receives)
+    holder = {}
+
+    def nccl_step(mark):
+        loc = f.fp8_linear(x, wqs, wss, bs)
+        if mark is not None:
+            mark.record(stream)
+        holder["nccl"] = S.gather_columns(loc, world)
+
+    t_nccl, t_comp = timed(nccl_step, args.steps)
+    ok_nccl = bool(torch.equal(holder.pop("nccl"), full))
+    capi = CApi()
+    work = torch.empty(capi.workspace_size(wl.M, wl.K), dtype=torch.uint8, device=dev)
+    fused = S.FusedColumnParallel(wl.M, wl.N, torch.bfloat16, dev, peer=capi)
+    try:
+        def fused_step(mark):
+            holder["fused"] = fused(x, wqs, wss, bs, capi, workspace=work)
+            if mark is not None:
+                mark.record(stream)
+
+        t_fused, _ = timed(fused_step, args.steps)
+        ok_fused = bool(torch.equal(holder.pop("fused"), full))
+        torch.cuda.synchronize(dev)
+    finally:
+        fused.close()
+    t_nccl, t_comp, t_fused = _max_over_ranks([t_nccl, t_comp, t_fused], world, dev)
+    ok = _max_over_ranks([0.0 if ok_nccl else 1.0, 0.0 if ok_fused else 1.0], world, dev)
+    link = 770.0  # measured peer copy GB/s per direction on this pool's B200s
+    res.update({
+        "parallelism": f"N-shard x{world} (column parallel, x replicated)",
+        "scaling": "strong",
+        "peer_bytes_per_rank": peer_bytes,
+        "nccl": {"ms_per_step": round(t_nccl, 4),
+                 "value": round(wl.flops / (t_nccl * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                 "compute_ms": round(t_comp, 4), "allgather_ms": round(t_nccl - t_comp, 4),
+                 "allgather_gbs": round(peer_bytes / ((t_nccl - t_comp) * 1e-3) / 1e9, 1),
+                 "bitexact_vs_unsharded": ok[0] == 0.0},
+        "fused": {"ms_per_step": round(t_fused, 4),
+                  "value": round(wl.flops / (t_fused * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                  "peer_store_gbs": round(peer_bytes / (t_fused * 1e-3) / 1e9, 1),
+                  "bitexact_vs_unsharded": ok[1] == 0.0,
+                  "roofline": {"bound": "nvlink", "peak_gbs_per_direction": link,
+                               "target_ms": round(max(peer_bytes / (link * 1e9) * 1e3,
+                                                      t_comp), 4),
+                               "frac": round(max(peer_bytes / (link * 1e9) * 1e3, t_comp)
+                                             / t_fused, 4)}},
+        "how": f"{args.steps} eager steps each, CUDA events per step, max over ranks; "
+               "compute_ms: the rank's column-block linear alone; fused roofline: the "
+               "slower of the rank's compute and its peer bytes at 770 GB/s per direction",
+    })
+    return res
 
 
 def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> dict:
@@ -489,9 +726,8 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
     rotating operand sets (inputs larger than L2), averaged per launch. ``fmt`` "mx" / "nv":
     the MXFP8 / NVFP4 ops (mxfp8_linear, mxfp8_gemm, quantize_mxfp8 / the nvfp4 ones)."""
     import fp8linear_b200 as f
-    from fp8linear_b200.workloads import WORKLOADS
 
-    wl = WORKLOADS[name]
+    wl = _workloads().WORKLOADS[name]
     dev = torch.device("cuda", torch.cuda.current_device())
     n_sets = set_count(per_set_bytes(wl), dev)
     sets = operand_sets(wl, n_sets, fmt=fmt)
@@ -555,9 +791,7 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
 
 def reference_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> dict:
     """Device time of the reference's own compiled ops on one workload."""
-    from fp8linear_b200.workloads import WORKLOADS
-
-    wl = WORKLOADS[name]
+    wl = _workloads().WORKLOADS[name]
 
     class A:  # the knobs reference_gpu_timing reads
         pass
@@ -574,7 +808,7 @@ def reference_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> 
 
 
 def run_sweep(args):
-    from fp8linear_b200.workloads import WORKLOADS
+    WORKLOADS = _workloads().WORKLOADS
 
     torch.cuda.set_device(0)
     names = args.sweep.split(",") if args.sweep != "all" else list(WORKLOADS)
@@ -598,9 +832,10 @@ def run_nshard(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     import fp8linear_b200 as f
     from fp8linear_b200 import sharding as S
-    from fp8linear_b200.workloads import WORKLOADS, make_weight, make_x
 
-    wl = WORKLOADS[args.workload]
+    W = _workloads()
+    make_weight, make_x = W.make_weight, W.make_x
+    wl = W.WORKLOADS[args.workload]
     x = make_x(wl, gen_device="cuda")                 # replicated activations
     w, b = make_weight(wl, gen_device="cuda")
     wq, ws = f.quantize_weight(w)
@@ -682,13 +917,17 @@ def run_nshard(args):
 
 
 def run_reference(args):
+    """The reference arm: the reference's path on the host CPU (the oracle port, all host
+    threads), on this arm's workload, metric and config. Under torchrun rank 0 alone runs
+    it; each step is one rank's share of the job (all ``M_per_gpu`` token rows), so the
+    rate is what the host's cores sustain on the job. Nothing of this package is
+    imported: only the oracle's libraries (and, for ``gpu_reference``, the reference's
+    own compiled ops) are loaded."""
     world, rank, local = dist_env()
     if rank != 0:
         return
-    from fp8linear_b200.workloads import WORKLOADS
-
-    wl = WORKLOADS[args.workload]
-    rows = args.cpu_rows
+    wl = _workloads().WORKLOADS[args.workload]
+    rows = args.ref_rows if args.ref_rows > 0 else wl.M
     threads = os.cpu_count() or 1
     st = cpu_reference_runner(wl, rows, threads=threads)
     for _ in range(args.warmup):
@@ -700,6 +939,10 @@ def run_reference(args):
         times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
     value = 2 * rows * wl.N * wl.K / per / 1e12
+    sample = (f"{rows} of {wl.M} token rows per step of {wl.name} (one rank's share"
+              f"{'' if world == 1 else f' of {world}'}); the reference has no CPU kernels, so "
+              "its path on a CPU is the CPU restatement (oracle port): per-token e4m3 quant, "
+              "fp32 matmul of decoded codes, dequant + bias")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -713,15 +956,10 @@ def run_reference(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "e4m3",
-        "data": "synthetic (seeded FLUX-shaped tensors)",
-        "config": {"workload": wl.name, "M_per_gpu": wl.M, "K": wl.K, "N": wl.N,
-                   "sample_rows": rows, "x": "bf16"},
+        "data": DATA,
+        "config": bench_config(wl, world),
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"{rows} of {wl.M} token rows per step of {wl.name}; the "
-                                   "reference has no CPU kernels, so its path is the CPU "
-                                   "restatement (oracle port): per-token e4m3 quant, fp32 "
-                                   "matmul of decoded codes, dequant + bias"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -744,7 +982,8 @@ def reference_gpu_timing(wl, args, fmt: str = "fp8"):
         return {"unavailable": f"reference ops failed to load: {e}"}
     if ref is None:
         return {"unavailable": "oracle/_ref not built"}
-    from fp8linear_b200.workloads import make_weight, make_x
+    W = _workloads()
+    make_weight, make_x = W.make_weight, W.make_x
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -808,9 +1047,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="flux_qkv")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=128)
+    ap.add_argument("--cpu-rows", type=int, default=128,
+                    help="token rows of the cpu_baseline sample in this arm's line")
+    ap.add_argument("--ref-rows", type=int, default=0,
+                    help="token rows per step of the reference arm (0: all M_per_gpu rows)")
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-4 (strong M-shard) and config-5 (N-shard) legs")
     ap.add_argument("--mode", choices=["mshard", "nshard"], default="mshard",
                     help="multi-GPU split: token rows (default, no collective) or output "
                          "channels with an NCCL all-gather")

@@ -49,7 +49,14 @@ SIGNATURES = {
     "fp8lin_selftest_watchdog": (_I, [ctypes.c_uint, ctypes.POINTER(ctypes.c_uint), _P]),
     "fp8lin_fp8_linear_allgather": (_I, [_P, _I, _P, _P, _P, _I, ctypes.POINTER(ctypes.c_void_p),
                                          _I, _I, _I64, _I64, _I64, _I64, _P, _SZ, _P]),
+    "fp8lin_peer_buffer_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
+    "fp8lin_peer_buffer_open": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "fp8lin_peer_buffer_close": (_I, [_P]),
+    "fp8lin_peer_buffer_free": (_I, [_P]),
 }
+
+# FP8LIN_PEER_HANDLE_BYTES in the header
+PEER_HANDLE_BYTES = 64
 
 # fp8lin_fp8_linear_noalloc's fixed scratch (FP8LIN_NOALLOC_SCRATCH_BYTES in the header)
 NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024
@@ -301,6 +308,42 @@ class CApi:
             arr, len(out_ptrs), DTYPE[out_dtype], M, N, K, ldo, workspace.data_ptr(),
             workspace.numel(), self._stream(x))
         self._check(rc, "fp8lin_fp8_linear_allgather")
+
+    # -- peer buffers (one process per GPU; CUDA IPC mappings, no multicast object)
+    def peer_alloc(self, nbytes: int) -> tuple[int, bytes]:
+        """Allocate ``nbytes`` on the current device; returns (device address, handle)."""
+        ptr = ctypes.c_void_p()
+        h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+        self._check(self.lib.fp8lin_peer_buffer_alloc(nbytes, ctypes.byref(ptr), h),
+                    "fp8lin_peer_buffer_alloc")
+        return int(ptr.value), h.raw
+
+    def peer_open(self, handle: bytes) -> int:
+        """Map another process's buffer; returns its address in this process."""
+        if len(handle) != PEER_HANDLE_BYTES:
+            raise ValueError(f"peer handle must be {PEER_HANDLE_BYTES} bytes")
+        ptr = ctypes.c_void_p()
+        self._check(self.lib.fp8lin_peer_buffer_open(handle, ctypes.byref(ptr)),
+                    "fp8lin_peer_buffer_open")
+        return int(ptr.value)
+
+    def peer_close(self, ptr: int) -> None:
+        self._check(self.lib.fp8lin_peer_buffer_close(ptr), "fp8lin_peer_buffer_close")
+
+    def peer_free(self, ptr: int) -> None:
+        self._check(self.lib.fp8lin_peer_buffer_free(ptr), "fp8lin_peer_buffer_free")
+
+    @staticmethod
+    def peer_tensor(ptr: int, nbytes: int, device: torch.device) -> torch.Tensor:
+        """A uint8 tensor over ``nbytes`` at device address ``ptr`` (not owned: the
+        memory lives until peer_free / peer_close)."""
+
+        class _Mem:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                        "data": (ptr, False), "version": 3, "strides": None}
+
+        with torch.cuda.device(device):
+            return torch.as_tensor(_Mem(), device=device)
 
     def selftest_watchdog(self, limit_us: int = 50_000) -> int:
         """Run the bounded-wait self-test; returns the recorded status (32 = the wait ran

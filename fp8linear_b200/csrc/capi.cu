@@ -1,9 +1,11 @@
 // capi.cu -- the extern "C" boundary (include/fp8linear_b200.h): argument checks that
 // mirror the reference's TORCH_CHECKs, workspace carving for the fused op, and the
-// thread-local error message. No allocation happens here.
+// thread-local error message. Only the peer-buffer set-up calls allocate (or map)
+// device memory; every operator call works in the caller's buffers.
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -464,6 +466,7 @@ struct HostStreams {
   cudaError_t err = cudaSuccess;
   cudaStream_t up = nullptr, comp = nullptr, down = nullptr;
   cudaEvent_t start = nullptr, up_done[2] = {}, comp_done[2] = {}, down_done[2] = {};
+  cudaEvent_t join[3] = {};  // error path: the caller's stream waits on all three streams
 };
 
 // The three streams and the events of the current device (created once, kept for the
@@ -487,6 +490,8 @@ HostStreams *host_streams(std::string *why) {
         (h.err = cudaStreamCreateWithFlags(&h.comp, sf)) == cudaSuccess &&
         (h.err = cudaStreamCreateWithFlags(&h.down, sf)) == cudaSuccess &&
         (h.err = cudaEventCreateWithFlags(&h.start, ef)) == cudaSuccess) {
+      for (int i = 0; i < 3 && h.err == cudaSuccess; ++i)
+        h.err = cudaEventCreateWithFlags(&h.join[i], ef);
       for (int i = 0; i < 2 && h.err == cudaSuccess; ++i)
         if ((h.err = cudaEventCreateWithFlags(&h.up_done[i], ef)) == cudaSuccess &&
             (h.err = cudaEventCreateWithFlags(&h.comp_done[i], ef)) == cudaSuccess)
@@ -549,6 +554,7 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
   if (e == cudaSuccess) e = cudaStreamWaitEvent(h->comp, h->start, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(h->down, h->start, 0);
   const int64_t chunks = (M + rows - 1) / rows;
+  rc = FP8LIN_OK;
   for (int64_t i = 0; i < chunks && e == cudaSuccess; ++i) {
     const int s = static_cast<int>(i & 1);
     const int64_t r0 = i * rows;
@@ -569,8 +575,11 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
     if (e != cudaSuccess) break;
     GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
                bias ? bias_dtype : kNone, obuf[s], out_dtype, mr, N, K};
+    // A ragged last chunk of a multi-chunk call takes the CTA-pair kernel like the full
+    // chunks, so every row is summed in the order the whole-M call uses.
+    a.pairs_only = chunks > 1;
     rc = launch_gemm(a, h->comp, true);
-    if (rc != FP8LIN_OK) return rc;  // launch_gemm set the message
+    if (rc != FP8LIN_OK) break;  // launch_gemm set the message
     e = cudaEventRecord(h->comp_done[s], h->comp);
     // download chunk i
     step = "download";
@@ -582,14 +591,30 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
   }
   // the caller's stream continues once the last download is done (it follows every
   // earlier copy and kernel of the call)
-  if (e == cudaSuccess) {
+  if (e == cudaSuccess && rc == FP8LIN_OK) {
     step = "ordering";
     e = cudaStreamWaitEvent(user, h->down_done[(chunks - 1) & 1], 0);
+    if (e == cudaSuccess) return FP8LIN_OK;
   }
-  if (e != cudaSuccess)
-    return fail(FP8LIN_ERR_CUDA, std::string("fp8_linear_host: ") + step + ": " +
-                                     cudaGetErrorString(e));
-  return FP8LIN_OK;
+  // Failed part-way: copies and kernels of earlier chunks may still be queued on the
+  // library's streams and still target the caller's host buffers and workspace. The
+  // caller's stream waits for all three streams before the error is returned, so work
+  // the caller orders after this call (a free, a reuse of out_host) follows them.
+  const std::string msg = rc != FP8LIN_OK
+                              ? std::string(g_last_error)
+                              : std::string("fp8_linear_host: ") + step + ": " +
+                                    cudaGetErrorString(e);
+  cudaEvent_t joins[3] = {h->join[0], h->join[1], h->join[2]};
+  cudaStream_t lanes[3] = {h->up, h->comp, h->down};
+  bool joined = true;
+  for (int j = 0; j < 3; ++j)
+    joined = joined && cudaEventRecord(joins[j], lanes[j]) == cudaSuccess &&
+             cudaStreamWaitEvent(user, joins[j], 0) == cudaSuccess;
+  if (!joined) {
+    // the event path itself failed: wait on the host instead
+    for (int j = 0; j < 3; ++j) cudaStreamSynchronize(lanes[j]);
+  }
+  return fail(rc != FP8LIN_OK ? rc : FP8LIN_ERR_CUDA, msg);
 }
 
 int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, const float *w_scale,
@@ -631,6 +656,64 @@ int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, cons
   a.n_peers = n_outs - 1;
   a.peers = outs + 1;
   return launch_gemm(a, s, true);
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == FP8LIN_PEER_HANDLE_BYTES,
+              "CUDA IPC handle size differs from FP8LIN_PEER_HANDLE_BYTES");
+
+int fp8lin_peer_buffer_alloc(size_t bytes, void **ptr, unsigned char *handle_out) {
+  clear_error();
+  if (!ptr || !handle_out || bytes == 0)
+    return fail(FP8LIN_ERR_INVALID_ARGUMENT, "peer_buffer_alloc: null pointer or zero size");
+  *ptr = nullptr;
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("peer_buffer_alloc: cudaMalloc: ") +
+                                     cudaGetErrorString(e));
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(FP8LIN_ERR_CUDA, std::string("peer_buffer_alloc: cudaIpcGetMemHandle: ") +
+                                     cudaGetErrorString(e));
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return FP8LIN_OK;
+}
+
+int fp8lin_peer_buffer_open(const unsigned char *handle, void **ptr) {
+  clear_error();
+  if (!ptr || !handle) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "peer_buffer_open: null pointer");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void *p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("peer_buffer_open: cudaIpcOpenMemHandle: ") +
+                                     cudaGetErrorString(e));
+  *ptr = p;
+  return FP8LIN_OK;
+}
+
+int fp8lin_peer_buffer_close(void *ptr) {
+  clear_error();
+  if (!ptr) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "peer_buffer_close: null pointer");
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("peer_buffer_close: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
+}
+
+int fp8lin_peer_buffer_free(void *ptr) {
+  clear_error();
+  if (!ptr) return fail(FP8LIN_ERR_INVALID_ARGUMENT, "peer_buffer_free: null pointer");
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess)
+    return fail(FP8LIN_ERR_CUDA, std::string("peer_buffer_free: ") + cudaGetErrorString(e));
+  return FP8LIN_OK;
 }
 
 int fp8lin_selftest_watchdog(unsigned int limit_us, unsigned int *status, void *stream) {

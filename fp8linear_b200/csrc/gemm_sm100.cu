@@ -904,7 +904,7 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
       set_error("block-scaled gemm: peer outputs are not supported");
       return 2;
     }
-    if (a.M <= 2 * gemm::BM) {
+    if (a.M <= 2 * gemm::BM && !a.pairs_only) {
       const int rc = launch_gemm_small(a, stream, pdl);
       if (rc != kSmallDeclined) return rc;
     }
@@ -914,11 +914,12 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   // Few tokens: stream the weights with swap-AB split-K tiles (M <= 128; up to 256 where
   // the kernel gets a K-split). Otherwise CTA pairs with 256-row tiles (or single CTAs
   // with 128-row tiles for peer outputs at M <= 128).
-  if (a.M <= 2 * gemm::BM && a.n_peers == 0) {
+  if (a.M <= 2 * gemm::BM && a.n_peers == 0 && !a.pairs_only) {
     const int rc = launch_gemm_small(a, stream, pdl);
     if (rc != kSmallDeclined) return rc;
   }
-  if (a.M <= gemm::BM) return gemm::launch_shape<1, gemm::kFmtE4M3>(a, dev, stream, pdl);
+  if (a.M <= gemm::BM && !a.pairs_only)
+    return gemm::launch_shape<1, gemm::kFmtE4M3>(a, dev, stream, pdl);
   return gemm::launch_shape<2, gemm::kFmtE4M3>(a, dev, stream, pdl);
 }
 

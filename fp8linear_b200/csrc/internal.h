@@ -88,6 +88,9 @@ struct GemmArgs {
   bool nv = false;
   const uint8_t *xsf = nullptr;
   const uint8_t *wsf = nullptr;
+  // Skip the few-token kernel and run CTA pairs at any M (same per-element summation
+  // order as every larger M): the row chunks of one host-buffer call.
+  bool pairs_only = false;
 };
 constexpr int kMaxPeers = 7;
 // Launches the tcgen05 GEMM + fused epilogue. `pdl` launches it as a programmatic

@@ -85,39 +85,120 @@ def column_parallel_linear(x: torch.Tensor, wq_shard: torch.Tensor, ws_shard: to
 class FusedColumnParallel:
     """N-shard linear with the all-gather fused into the GEMM epilogue.
 
-    Every rank owns an [M, N_total] output buffer in symmetric memory (mapped into every
-    other rank's address space). ``__call__`` runs the fused op on this rank's channel
-    block: each output box is stored to this GPU's buffer and, with P2P stores over
-    NVLink, to every peer's buffer at this rank's column offset; a one-element NCCL
-    all-reduce then orders every rank's writes before anyone reads the result. No
-    separate all-gather or interleave copy runs.
+    Every rank allocates two ``[M, N_total]`` output buffers as peer memory (plain CUDA
+    IPC mappings over NVLink through the C ABI's ``fp8lin_peer_buffer_*``; no multicast
+    object) and maps every other rank's two. Call j writes buffer ``j % 2``: the
+    epilogue stores each output box to this GPU's buffer and, with P2P stores, to every
+    peer's buffer at this rank's column offset; a one-element all-reduce on the stream
+    then orders every rank's writes before anyone reads the result. No separate
+    all-gather or interleave copy runs.
+
+    Lifetime of a result: the tensor that call j returns is the buffer that call j + 2
+    rewrites, on every rank. No rank starts call j + 2 before the all-reduce of call
+    j + 1 has completed everywhere, and that all-reduce follows, on each rank's stream,
+    everything the rank enqueued before making call j + 1. So a result stays intact for
+    every read enqueued before the call after next; ``.clone()`` it to keep it longer.
+
+    ``peer`` provides the buffer set-up (``peer_alloc``, ``peer_open``, ``peer_close``,
+    ``peer_free``, ``peer_tensor``) and the fused op (``fp8_linear_allgather``); it
+    defaults to the C ABI binding. ``close()`` releases the buffers collectively.
     """
 
     def __init__(self, M: int, N_total: int, dtype: torch.dtype, device: torch.device,
-                 group=None):
-        import torch.distributed._symmetric_memory as symm
-
+                 group=None, peer=None):
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
-        self.M, self.N_total = M, N_total
+        self.M, self.N_total, self.dtype, self.device = M, N_total, dtype, torch.device(device)
         column_range(N_total, self.world, self.rank)  # validates the split
-        self.buf = symm.empty(M, N_total, dtype=dtype, device=device)
-        self.hdl = symm.rendezvous(self.buf, self.group)
-        offset = self.buf.data_ptr() - self.hdl.buffer_ptrs[self.rank]
-        self.bases = [int(b) + offset for b in self.hdl.buffer_ptrs]
-        self.flag = torch.zeros(1, device=device)
+        if peer is None:
+            from .capi import CApi
 
-    def out_ptrs(self) -> list[int]:
-        """This rank's first output column in every rank's buffer, own buffer first."""
+            peer = CApi()
+        self.peer = peer
+        self.elem = torch.empty((), dtype=dtype).element_size()
+        self.nbytes = M * N_total * self.elem
+        self.local: list[int] = []        # this rank's two buffers
+        self.opened: list[int] = []       # peers' buffers mapped here
+        self.bases: list[list[int]] = []  # per buffer: every rank's base address, by rank
+        self.views: list[torch.Tensor] = []
+        err = None
+        try:
+            for _ in range(2):
+                ptr, handle = self.peer.peer_alloc(self.nbytes)
+                self.local.append(ptr)
+                handles = [None] * self.world
+                dist.all_gather_object(handles, handle, group=self.group)
+                bases = []
+                for r in range(self.world):
+                    if r == self.rank:
+                        bases.append(ptr)
+                    else:
+                        q = self.peer.peer_open(handles[r])
+                        self.opened.append(q)
+                        bases.append(q)
+                self.bases.append(bases)
+                self.views.append(self.peer.peer_tensor(ptr, self.nbytes, self.device)
+                                  .view(dtype).view(M, N_total))
+        except Exception as e:  # every rank learns of a failed set-up before going on
+            err = e
+        ok = torch.tensor([0 if err is not None else 1], dtype=torch.int32,
+                          device=self._coll_device())
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        self.calls = 0
+        self.closed = False
+        self.flag = torch.zeros(1, device=self._coll_device())
+        if int(ok.item()) != 1:
+            self._release(collective=False)
+            raise RuntimeError(f"peer buffer set-up failed on a rank: {err!r}")
+
+    def _coll_device(self) -> torch.device:
+        return torch.device("cpu") if dist.get_backend(self.group) == "gloo" else self.device
+
+    def out_ptrs(self, buf: int) -> list[int]:
+        """This rank's first output column in every rank's buffer ``buf``, own first."""
         n_local = self.N_total // self.world
-        col = self.rank * n_local * self.buf.element_size()
+        col = self.rank * n_local * self.elem
         order = [self.rank] + [r for r in range(self.world) if r != self.rank]
-        return [self.bases[r] + col for r in order]
+        return [self.bases[buf][r] + col for r in order]
 
-    def __call__(self, x, wq_shard, ws_shard, bias_shard, capi, workspace=None):
-        capi.fp8_linear_allgather(x, wq_shard, ws_shard, bias_shard, self.out_ptrs(),
-                                  ldo=self.N_total, workspace=workspace)
+    def __call__(self, x, wq_shard, ws_shard, bias_shard, capi=None, workspace=None):
+        if self.closed:
+            raise RuntimeError("FusedColumnParallel used after close()")
+        buf = self.calls % 2
+        self.calls += 1
+        op = capi if capi is not None else self.peer
+        op.fp8_linear_allgather(x, wq_shard, ws_shard, bias_shard, self.out_ptrs(buf),
+                                ldo=self.N_total, workspace=workspace)
         if self.world > 1:
             dist.all_reduce(self.flag, group=self.group)
-        return self.buf
+        return self.views[buf]
+
+    def _release(self, collective: bool) -> None:
+        self.views = []
+        if collective:
+            # every rank is done with the peers' buffers before any mapping goes away
+            if self.device.type == "cuda":
+                torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+        for q in self.opened:
+            self.peer.peer_close(q)
+        self.opened = []
+        if collective:
+            dist.barrier(group=self.group)  # no rank maps this rank's buffers any more
+        for p in self.local:
+            self.peer.peer_free(p)
+        self.local = []
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every rank calls
+        it, with none of the buffers' readers still in flight)."""
+        if not self.closed:
+            self.closed = True
+            self._release(collective=True)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

@@ -4,8 +4,8 @@
  * Plain pointers and sizes only; no framework types cross this boundary. Every
  * device pointer is a CUDA device address on the calling thread's current device,
  * and every call is asynchronous on `stream` (a cudaStream_t passed as void*;
- * NULL means the legacy default stream). No call synchronises the host or
- * allocates device memory.
+ * NULL means the legacy default stream). Apart from the peer-buffer set-up calls
+ * (fp8lin_peer_buffer_*), no call synchronises the host or allocates device memory.
  *
  * Each entry point replaces one operator of drbh/fp8linear (paths relative to the
  * reference project root); the argument meaning and error conditions follow the
@@ -298,13 +298,15 @@ FP8LIN_API int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq,
  * multi-GPU code). This rank holds N output channels (wq/w_scale/bias rows) of a wider
  * [M, ldo] output; each output box the epilogue produces is written to outs[0] (this
  * GPU, TMA store) and to outs[1..n_outs-1] (other GPUs' buffers mapped into this process,
- * e.g. peer or symmetric memory, with 16-byte P2P stores), so the gather overlaps the
- * math and no separate collective or interleave copy runs.
+ * e.g. with fp8lin_peer_buffer_open, written with 16-byte P2P stores), so the gather
+ * overlaps the math and no separate collective or interleave copy runs.
  *   outs[i]: pointer to this rank's first output column in buffer i; rows of ldo
  *            elements; all buffers 16-byte aligned; N and ldo multiples of 8
  *   n_outs:  1..8 (1 = this GPU only)
  * Other arguments as fp8lin_fp8_linear. The caller orders the peers' reads after every
- * rank's call completes (e.g. a device-side barrier on the stream).
+ * rank's call completes (e.g. a one-element all-reduce on the stream after the call),
+ * and orders each call's writes after the peers' last reads of the buffer it writes
+ * (e.g. two buffers used in turn, so the all-reduce of the call in between covers it).
  */
 FP8LIN_API int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq,
                                            const float *w_scale, const void *bias,
@@ -312,6 +314,30 @@ FP8LIN_API int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const voi
                                            int out_dtype, int64_t M, int64_t N, int64_t K,
                                            int64_t ldo, void *workspace,
                                            size_t workspace_bytes, void *stream);
+
+/*
+ * Peer buffers for fp8lin_fp8_linear_allgather when every GPU is driven by its own
+ * process (one process per GPU). No counterpart in the reference (it has no multi-GPU
+ * code). Plain CUDA peer memory over NVLink: the buffers are ordinary device
+ * allocations mapped into the other processes with CUDA IPC handles; no NVLink
+ * multicast object is created or bound.
+ *   fp8lin_peer_buffer_alloc: allocates `bytes` on the current device (256-byte
+ *     aligned) into *ptr and writes its FP8LIN_PEER_HANDLE_BYTES-byte handle to
+ *     handle_out, for the other processes of the node.
+ *   fp8lin_peer_buffer_open: maps another process's buffer from its handle into this
+ *     process (current device) and returns the address this process's kernels use for
+ *     it. A process cannot open its own handle.
+ *   fp8lin_peer_buffer_close: unmaps a buffer opened here.
+ *   fp8lin_peer_buffer_free: frees a buffer allocated here; call it only after every
+ *     process that opened it has closed it.
+ * These are set-up calls: they allocate, map or free device memory and may synchronise
+ * the device. Not for use during stream capture.
+ */
+#define FP8LIN_PEER_HANDLE_BYTES 64
+FP8LIN_API int fp8lin_peer_buffer_alloc(size_t bytes, void **ptr, unsigned char *handle_out);
+FP8LIN_API int fp8lin_peer_buffer_open(const unsigned char *handle, void **ptr);
+FP8LIN_API int fp8lin_peer_buffer_close(void *ptr);
+FP8LIN_API int fp8lin_peer_buffer_free(void *ptr);
 
 /*
  * Size of the device scratch array fp8lin_fp8_linear_noalloc works in (64 MiB).
@@ -325,8 +351,7 @@ FP8LIN_API int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const voi
  * FP8LIN_NOALLOC_SCRATCH_BYTES inside the library instead. Meant for hosts that give
  * an op only its input and output buffers (plugin/custom-op interfaces whose device
  * memory is owned by the host's pool) or cannot afford cudaMalloc's implicit
- * synchronisation. No counterpart in the reference (its fp8_linear allocates with
- * torch::empty, csrc/fp8_gemm.cu:162-166).
+ * synchronisation. No counterpart in the reference.
  *   Arguments, results and errors as fp8lin_fp8_linear, plus FP8LIN_ERR_WORKSPACE when
  *   fp8lin_linear_workspace_size(M, K) > FP8LIN_NOALLOC_SCRATCH_BYTES.
  *   All calls on a device share the one array: calls whose GPU work overlaps race on

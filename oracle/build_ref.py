@@ -4,8 +4,10 @@ Test infrastructure only. The product never imports, links or runs anything
 built here; only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
 reference leg may load it, and only as a checker.
 
-The reference sources are compiled where they lie (``/root/reference/csrc`` and
-``/root/reference/torch-ext``); nothing is copied into this repository. The one
+The reference sources are compiled where they lie (``<ref>/csrc`` and
+``<ref>/torch-ext`` of a drbh/fp8linear checkout); nothing is copied into this
+repository. ``<ref>`` is ``$FP8LINEAR_REF_ROOT`` when set, else a checkout named
+``reference`` next to this repository's root directory. The one
 header the reference binding needs and does not ship (``registration.h``, which
 its kernel-builder toolchain generates) is replaced by ``oracle/ref_shim``.
 
@@ -27,8 +29,9 @@ import os
 import sys
 from pathlib import Path
 
-REF_ROOT = Path(os.environ.get("FP8LINEAR_REF_ROOT", "/root/reference"))
 HERE = Path(__file__).resolve().parent
+# a drbh/fp8linear checkout: $FP8LINEAR_REF_ROOT, else <repo>/../reference
+REF_ROOT = Path(os.environ.get("FP8LINEAR_REF_ROOT") or HERE.parent.parent / "reference")
 OUT_DIR = HERE / "_ref"
 NAME = "fp8linear_ref"
 SO_PATH = OUT_DIR / f"{NAME}.so"

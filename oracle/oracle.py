@@ -315,6 +315,25 @@ def np_quantize_rows(x16: np.ndarray, dtype: int = BF16):
     return np_e4m3_encode(c, saturate=True), sc
 
 
+def torch_quantize_rows(x):
+    """Per-token quantization of a CPU tensor x [M, K] (bf16/fp16) with multi-threaded
+    torch ops: the reference's rule (csrc/quantize.cu:52-72) as its torch emulation
+    writes it. amax in fp32, sc = max(amax / 448, 1e-12), inv = 1 / sc (IEEE fp32
+    divides), codes = e4m3(clamp(x * inv, -448, 448)) with torch's round-to-nearest-even
+    cast. Bit-identical to np_quantize_rows on finite inputs (torch's amax propagates a
+    NaN where the kernel's fmaxf ignores it). Returns (codes as torch.float8_e4m3fn,
+    scales fp32)."""
+    import torch
+
+    xf = x.float()
+    amax = xf.abs().amax(dim=1)
+    lim = float(E4M3_MAX)
+    sc = torch.clamp_min(amax / lim, float(SCALE_FLOOR))
+    inv = 1.0 / sc
+    q = xf.mul_(inv[:, None]).clamp_(-lim, lim).to(torch.float8_e4m3fn)
+    return q, sc
+
+
 def _np_round_to(f: np.ndarray, dtype: int) -> np.ndarray:
     f = np.ascontiguousarray(f, np.float32)
     if dtype == BF16:

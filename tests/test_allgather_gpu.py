@@ -1,9 +1,10 @@
 """Fused column-parallel linear (fp8lin_fp8_linear_allgather) on one GPU: extra local
 buffers stand in for the peers' output buffers, so the epilogue's peer-store path is
 checked without a second GPU. Every copy of this rank's column block must hold the same
-bits, within OUT_TOL of the plain fused linear on the shard (which, for M <= 512, may run
-the split-K few-token kernel, whose fp32 summation order differs from the CTA-pair
-kernel's), and no column outside the block may change. With a
+bits, and no column outside the block may change. Against the plain fused linear on the
+shard the block is bit-exact when both run the CTA-pair kernel (M > 256); for M <= 256 the
+plain linear may run the split-K few-token kernel, whose fp32 summation order differs, so
+there the check is OUT_TOL. With a
 single buffer (no peers) the epilogue's paired stores write a column block of a wider
 row pitch (ldo > N)."""
 from __future__ import annotations
@@ -41,7 +42,10 @@ def test_allgather_epilogue_writes_every_copy(M, N_total, K, world, rank, single
                               b[s:e].contiguous(), ptrs, ldo=N_total)
     torch.cuda.synchronize()
     first = bufs[0][:, s:e]
-    assert max_rel(first.float().cpu(), ref.float().cpu()) <= OUT_TOL
+    if M > 256:
+        assert torch.equal(first, ref)
+    else:
+        assert max_rel(first.float().cpu(), ref.float().cpu()) <= OUT_TOL
     for t in bufs:
         assert torch.equal(t[:, s:e], first)
         outside = torch.cat([t[:, :s].flatten(), t[:, e:].flatten()])

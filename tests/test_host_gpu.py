@@ -1,7 +1,9 @@
 """fp8_linear with x and out in host memory (fp8lin_fp8_linear_host): row chunks whose
 upload, kernels and download overlap on three streams must give the bits of the device
-path, for several chunk counts (one chunk, a ragged last chunk, the few-token kernel),
-dtypes, pageable buffers and calls back to back."""
+path, for several chunk counts (one chunk, a ragged last chunk of 488, 188 or 92 rows,
+the few-token kernel for a single short chunk), dtypes, pageable buffers and calls back
+to back. A ragged last chunk of a multi-chunk call runs the CTA-pair kernel like the
+whole-M call, so even a tail short enough for the few-token kernel keeps the bits."""
 from __future__ import annotations
 
 import pytest
@@ -32,6 +34,8 @@ def _weights(N, K, seed=0, dtype=torch.bfloat16):
 @pytest.mark.parametrize("M,N,K,dtype", [(4608, 1024, 3072, torch.bfloat16),
                                          (1000, 776, 512, torch.float16),
                                          (100, 256, 256, torch.bfloat16),
+                                         (700, 1024, 512, torch.bfloat16),
+                                         (4700, 512, 1024, torch.bfloat16),
                                          (1, 264, 96, torch.bfloat16)])
 def test_host_linear_matches_device(capi, M, N, K, dtype):
     wq, ws, b = _weights(N, K, seed=M, dtype=dtype)

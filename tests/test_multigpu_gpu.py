@@ -1,7 +1,9 @@
 """Multi-GPU column-parallel linear on 2 real GPUs (NCCL, one process per GPU): the
-fused epilogue all-gather (P2P stores into symmetric memory) and the NCCL all-gather
-path must both give the unsharded result bit for bit on every rank. Skipped where the
-machine has a single GPU."""
+fused epilogue all-gather (P2P stores into CUDA IPC peer buffers) and the NCCL
+all-gather path must both give the unsharded result bit for bit on every rank, also
+over repeated calls where rank 0 reads each result late (a device-side delay before
+its copy) while rank 1 runs its next call, whose stores land in rank 0's buffers.
+Skipped where the machine has a single GPU."""
 from __future__ import annotations
 
 import os
@@ -40,14 +42,25 @@ def _rank(rank, world, port, q):
         w = (torch.randn(N, K, generator=g) * 0.02).bfloat16().to(dev)
         b = (torch.randn(N, generator=g) * 0.02).bfloat16().to(dev)
         wq, ws = f.quantize_weight(w)
-        full = f.fp8_linear(x, wq, ws, b)
         wqs, wss, bs = S.shard_columns(wq, ws, b, world, rank)
-        nccl = S.column_parallel_linear(x, wqs, wss, bs, f.fp8_linear, world)
-        fused = S.FusedColumnParallel(M, N, torch.bfloat16, dev)
-        out = fused(x, wqs, wss, bs, CApi())
+        capi = CApi()
+        fused = S.FusedColumnParallel(M, N, torch.bfloat16, dev, peer=capi)
+        xs = [(x * (1.0 + 0.25 * j)).bfloat16() for j in range(5)]
+        fulls = [f.fp8_linear(xj, wq, ws, b) for xj in xs]
+        nccl_ok = [bool(torch.equal(S.column_parallel_linear(xj, wqs, wss, bs, f.fp8_linear,
+                                                              world), full))
+                   for xj, full in zip(xs[:2], fulls[:2])]
+        # No collective between rank 0's late read of call j and rank 1's call j + 1:
+        # rank 1's next stores reach rank 0's buffers while rank 0's stream still waits.
+        fused_ok = []
+        for xj, full in zip(xs, fulls):
+            out = fused(xj, wqs, wss, bs, capi)
+            if rank == 0:
+                torch.cuda._sleep(20_000_000)  # ~10 ms on the device before the read
+            fused_ok.append(bool(torch.equal(out.clone(), full)))
         torch.cuda.synchronize(dev)
-        q.put((rank, bool(torch.equal(nccl, full)), bool(torch.equal(out, full))))
-        del fused
+        fused.close()
+        q.put((rank, all(nccl_ok), all(fused_ok)))
     except Exception as e:  # report and leave the group
         q.put((rank, "error", repr(e)[:300]))
     finally:

@@ -117,3 +117,26 @@ def test_gemm_oracle_known_answer(oracle):
     out = oracle.c_gemm_dequant(xq, np.array([0.5], np.float32), wq, np.array([3.0], np.float32),
                                 np.array([np.float16(0.25)]).view(np.uint16), round_out=False)
     assert out[0, 0] == np.float32(48.25)
+
+
+@pytest.mark.parametrize("dt,code", [(torch.bfloat16, 0), (torch.float16, 1)])
+def test_quantize_rows_torch_twin_vs_numpy(oracle, dt, code):
+    """The multi-threaded torch twin (the timed CPU baseline's quantizer) gives the
+    numpy twin's codes and scales bit for bit on finite rows: FLUX-like outliers, a zero
+    row, values beyond 448 after scaling, tiny rows (subnormal codes), e4m3 midpoints."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(257, 1040, generator=g)
+    x[:, ::97] *= 50
+    x[3] = 0
+    x[4, :5] = 448 * 3
+    x[5] *= 1e-30 if dt == torch.bfloat16 else 1e-4
+    lut = torch.from_numpy(oracle.e4m3_decode_lut())
+    fin = lut[torch.isfinite(lut)].sort().values
+    mids = (fin[:-1] + fin[1:]) / 2
+    x[6, :mids.numel()] = mids
+    x[6, -1] = 448.0
+    xx = x.to(dt)
+    q, sc = oracle.torch_quantize_rows(xx)
+    nq, nsc = oracle.np_quantize_rows(xx.view(torch.int16).numpy().view(np.uint16), code)
+    assert np.array_equal(q.view(torch.uint8).numpy(), nq)
+    assert np.array_equal(sc.numpy().view(np.uint32), nsc.view(np.uint32))

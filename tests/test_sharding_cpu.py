@@ -1,10 +1,17 @@
 """Multi-rank sharding logic on CPU ranks (gloo, world size 2 and 4), with the oracle
 port as each rank's linear: sharded results must equal the unsharded result bit for
-bit. A rank that fails makes the others' collective end with an error, not a hang."""
+bit. A rank that fails makes the others' collective end with an error, not a hang.
+
+The fused all-gather's host logic (handle exchange, column offsets, the two buffers
+used in turn, the ordering all-reduce, collective release) runs here with a stand-in
+for the peer buffers: files mapped shared into every rank, written by a host-side
+"kernel" that stores this rank's block into every rank's buffer."""
 from __future__ import annotations
 
+import ctypes
 import os
 import socket
+import time
 from datetime import timedelta
 
 import numpy as np
@@ -44,6 +51,102 @@ def _inputs(M=96, K=64, N=48, seed=0):
     b = (torch.randn(N, generator=g) * 0.02).bfloat16()
     wq, ws = O.np_quantize_weight(w.view(torch.int16).numpy().view(np.uint16), O.BF16)
     return x, torch.from_numpy(wq), torch.from_numpy(ws), b
+
+
+class ShmPeer:
+    """Stand-in for the C ABI's peer buffers and fused op on CPU ranks: a buffer is a
+    file under ``root`` mapped shared (torch.from_file) into every rank that opens it;
+    its "handle" is the file name. ``fp8_linear_allgather`` computes this rank's block
+    with the oracle and writes it into every output pointer, row by row."""
+
+    def __init__(self, root: str):
+        self.root = root
+        self.maps: dict[int, tuple[torch.Tensor, str | None]] = {}
+        self.n = 0
+
+    def peer_alloc(self, nbytes):
+        path = os.path.join(self.root, f"buf_{os.getpid()}_{self.n}")
+        self.n += 1
+        t = torch.from_file(path, shared=True, size=nbytes, dtype=torch.uint8)
+        t.zero_()
+        self.maps[t.data_ptr()] = (t, path)
+        return t.data_ptr(), path.encode().ljust(64, b"\0")
+
+    def peer_open(self, handle):
+        path = handle.rstrip(b"\0").decode()
+        t = torch.from_file(path, shared=True, size=os.path.getsize(path), dtype=torch.uint8)
+        self.maps[t.data_ptr()] = (t, None)
+        return t.data_ptr()
+
+    def peer_close(self, ptr):
+        self.maps.pop(ptr)
+
+    def peer_free(self, ptr):
+        _, path = self.maps.pop(ptr)
+        os.unlink(path)
+
+    def peer_tensor(self, ptr, nbytes, device):
+        return self.maps[ptr][0]
+
+    def fp8_linear_allgather(self, x, wq, ws, bias, out_ptrs, ldo, workspace=None):
+        blk = oracle_linear(x, wq, ws, bias).bfloat16().contiguous()
+        M, n = blk.shape
+        for p in out_ptrs:
+            for m in range(M):
+                ctypes.memmove(p + m * ldo * 2, blk[m].data_ptr(), n * 2)
+
+
+def _fused_worker(rank, world, port, root, single_buffer, q):
+    """Four calls with different activations; rank 0 reads each result only after a
+    delay, while the other ranks go on to their next call (which stores into rank 0's
+    buffers). Every read must still see that call's own result."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    try:
+        from fp8linear_b200 import sharding as S
+
+        x0, wq, ws, b = _inputs(M=32, K=64, N=48)
+        wqs, wss, bs = S.shard_columns(wq, ws, b, world, rank)
+        fused = S.FusedColumnParallel(32, 48, torch.bfloat16, torch.device("cpu"),
+                                      peer=ShmPeer(root))
+        if single_buffer:  # the unsafe form: every call writes the same buffer
+            fused.out_ptrs = lambda buf, f=fused, o=S.FusedColumnParallel.out_ptrs: o(f, 0)
+            fused.views = [fused.views[0], fused.views[0]]
+        same = []
+        for j in range(4):
+            x = (x0 * (j + 1)).bfloat16()
+            out = fused(x, wqs, wss, bs)
+            if rank == 0:
+                time.sleep(0.3)
+            got = out.clone()
+            same.append(bool(torch.equal(got, oracle_linear(x, wq, ws, b).bfloat16())))
+        fused.close()
+        q.put((rank, "ok", tuple(same)))
+    except Exception as e:
+        q.put((rank, "error", type(e).__name__ + ": " + str(e)[:200]))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_fused(world, root, single_buffer=False):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, root, single_buffer, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    res = {}
+    while not q.empty():
+        r, status, payload = q.get()
+        res[r] = (status, payload)
+    return res
 
 
 def _worker(rank, world, port, mode, fail_rank, q):
@@ -131,3 +234,20 @@ def test_failed_rank_ends_collective_with_error():
     res = _run(2, "cols", fail_rank=1)
     assert res[1][0] == "error" and "injected" in res[1][1]
     assert res[0][0] == "error"
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_fused_column_parallel_buffers_in_turn(world, tmp_path):
+    """Every result read (rank 0 reading late) equals the unsharded result, and every
+    buffer file is freed by close()."""
+    res = _run_fused(world, str(tmp_path))
+    assert len(res) == world
+    assert all(v == ("ok", (True,) * 4) for v in res.values()), res
+    assert not any(tmp_path.iterdir())
+
+
+def test_fused_single_buffer_hazard_is_detected(tmp_path):
+    """The same test on the unsafe one-buffer form sees rank 0's late reads overwritten
+    by the other rank's next call: the check above is sensitive to the hazard."""
+    res = _run_fused(2, str(tmp_path), single_buffer=True)
+    assert res[0][0] == "ok" and not all(res[0][1]), res
