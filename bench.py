@@ -742,26 +742,28 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
         del g
         return ms
 
+    # the bandwidth-bound quantizer first: timed after seconds of full-power GEMM replays,
+    # a memory-bound kernel reads slow (the power-capped clocks outlast the GEMMs)
     extra = {}
     if fmt == "modulated":
-        fused = timed(lambda st: f.fp8_linear_modulated(st["x"], st["shift"], st["scale"], st["wq"],
-                                                        st["ws"], st["b"]))
-        gemm = timed(lambda st: f.fp8_gemm(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
         quant = timed(lambda st: f.layernorm_modulate_quantize_fp8(st["x"], st["shift"],
                                                                    st["scale"]))
-        unf = timed(lambda st: f.fp8_linear(unfused_modulation(st["x"], st["shift"], st["scale"]),
-                                            st["wq"], st["ws"], st["b"]))
         unq = timed(lambda st: f.quantize_fp8(unfused_modulation(st["x"], st["shift"],
                                                                  st["scale"])))
+        gemm = timed(lambda st: f.fp8_gemm(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
+        fused = timed(lambda st: f.fp8_linear_modulated(st["x"], st["shift"], st["scale"], st["wq"],
+                                                        st["ws"], st["b"]))
+        unf = timed(lambda st: f.fp8_linear(unfused_modulation(st["x"], st["shift"], st["scale"]),
+                                            st["wq"], st["ws"], st["b"]))
         extra = {"unfused_us": round(unf * 1e3, 2), "unfused_quant_us": round(unq * 1e3, 2)}
     else:
         lin_op, gemm_op, quant_op = {
             "fp8": (f.fp8_linear, f.fp8_gemm, f.quantize_fp8),
             "mx": (f.mxfp8_linear, f.mxfp8_gemm, f.quantize_mxfp8),
             "nv": (f.nvfp4_linear, f.nvfp4_gemm, f.quantize_nvfp4)}[fmt]
-        fused = timed(lambda st: lin_op(st["x"], st["wq"], st["ws"], st["b"]))
-        gemm = timed(lambda st: gemm_op(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
         quant = timed(lambda st: quant_op(st["x"]))
+        gemm = timed(lambda st: gemm_op(st["xq"], st["xs"], st["wq"], st["ws"], st["b"]))
+        fused = timed(lambda st: lin_op(st["x"], st["wq"], st["ws"], st["b"]))
     # quantizer bytes: read 2MK, write the codes (MK, NV MK/2) and the scales (4M fp32,
     # MK/32 e8m0, MK/16 ue4m3)
     mk = wl.M * wl.K
@@ -805,6 +807,60 @@ def reference_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> 
     else:
         r = {"workload": name, "format": fmt, **(r or {})}
     return r
+
+
+def run_launch_list(args):
+    """Eager launches for a per-kernel launch list: for each workload of ``--sweep``, a
+    marker kernel (torch.cuda._sleep), ``--steps`` calls of the fused linear over rotating
+    operand sets (ours: fp8_linear; ``--impl reference``: the reference's fp8_linear and
+    the .to(bf16) its Fp8Linear.forward applies), then another marker. Run under
+    ``ncu --metrics gpu__time_duration.sum``, the kernels between two markers are one
+    workload's calls, which splits the reference op into its quantizer, cuBLASLt GEMM,
+    dequant and cast kernels. One JSON line per workload names the order."""
+    W = _workloads()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    names = args.sweep.split(",") if args.sweep != "all" else list(W.WORKLOADS)
+    if args.impl == "reference":
+        from oracle import build_ref
+
+        ref = build_ref.load()
+        if ref is None:
+            print(json.dumps({"unavailable": "oracle/_ref not built"}))
+            return
+        qw = ref.quantize_weight
+
+        def lin(st):
+            return ref.fp8_linear(st["x"], st["wq"], st["ws"], st["b"]).to(st["x"].dtype)
+    else:
+        import fp8linear_b200 as f
+
+        qw = f.quantize_weight
+
+        def lin(st):
+            return f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"])
+    for n in names:
+        wl = W.WORKLOADS[n]
+        extra = 4 * wl.M * wl.N if args.impl == "reference" else 0  # its fp32 [M, N]
+        n_sets = set_count(per_set_bytes(wl) + extra, dev)
+        sets = []
+        for i in range(n_sets):
+            x = W.make_x(wl, seed=7919 * i, gen_device="cuda")
+            w, b = W.make_weight(wl, seed=7919 * i, gen_device="cuda")
+            wq, ws = qw(w)
+            sets.append({"x": x, "wq": wq, "ws": ws, "b": b})
+            del w
+        for i in range(args.warmup):
+            lin(sets[i % n_sets])
+        torch.cuda.synchronize(dev)
+        torch.cuda._sleep(1000)
+        outs = [lin(sets[i % n_sets]) for i in range(args.steps)]
+        torch.cuda._sleep(1000)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"workload": n, "impl": args.impl, "calls": args.steps,
+                          "sets": n_sets}), flush=True)
+        del sets, outs
+        torch.cuda.empty_cache()
 
 
 def run_sweep(args):
@@ -1067,9 +1123,14 @@ def main():
     ap.add_argument("--sweep", default="",
                     help="'all' or comma-separated workloads: one JSON line of per-kernel "
                          "device times per workload (not the driver's line)")
+    ap.add_argument("--launch-list", action="store_true",
+                    help="with --sweep: eager calls between marker kernels, for an ncu "
+                         "per-kernel launch list (no timing printed)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # the timing rules ask for at least 3 warm-up steps
-    if args.sweep:
+    if args.sweep and args.launch_list:
+        run_launch_list(args)
+    elif args.sweep:
         run_sweep(args)
     elif args.mode == "nshard" and args.impl != "reference":
         run_nshard(args)

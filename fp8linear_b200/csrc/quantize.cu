@@ -21,6 +21,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "internal.h"
@@ -203,7 +204,10 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const T *__restric
                                                               float *__restrict__ scale,
                                                               int64_t M, int K, int tpr,
                                                               int trigger) {
-  if (trigger) ptx::grid_launch_dependents();
+  // trigger bit 0: let the dependent grid launch now; bit 1: this grid is itself a
+  // programmatic dependent and waits for its prerequisite before touching memory
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   __shared__ uint32_t red[32];
   const int t_in_row = threadIdx.x % tpr;
   const int row_in_cta = threadIdx.x / tpr;
@@ -269,13 +273,208 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const T *__restric
   if (t_in_row == 0) scale[row] = sc;
 
   uint8_t *qr = xq + row * static_cast<int64_t>(K);
+  if (finite) {  // CTA-uniform: one conversion per value, not both and a select
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int j = t_in_row + i * tpr;
-    if (j < nvec)
-      *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) =
-          finite ? quant8_fast<T>(v[i], inv) : quant8_clamp<T>(v[i], inv);
+    for (int i = 0; i < VPT; ++i) {
+      const int j = t_in_row + i * tpr;
+      if (j < nvec)
+        *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) = quant8_fast<T>(v[i], inv);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int j = t_in_row + i * tpr;
+      if (j < nvec)
+        *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) = quant8_clamp<T>(v[i], inv);
+    }
   }
+}
+
+// ---------------------------------------------------------------- pipelined kernel
+//
+// Persistent and row-pipelined: a group of WPR warps owns rows g, g + G, g + 2G, ... (G
+// groups in the grid) and keeps two rows in registers: the 16-byte loads of its next row
+// are issued before the current row is reduced, converted and stored, so every group
+// has a row in flight while it works and the grid never drains between waves. Thread t
+// of a group holds vectors t + i * 32 * WPR (i < VPL) of a row: each warp load covers
+// 512 contiguous bytes. The amax of a row spanning several warps is exchanged through
+// shared memory under a named barrier of the group's threads (one barrier per row; the
+// exchange slots alternate by row so a slot is rewritten only after every warp of the
+// group has passed the next row's barrier). The fast/slow (non-finite) decision is made
+// per row from the group's maximum, so the slow path's barriers stay group-uniform.
+template <typename T, int VPL>
+__device__ __forceinline__ void pipe_load(uint4 (&v)[VPL], const T *x, int64_t row, int64_t M,
+                                          int K, int t, int stride) {
+  if (row >= M) return;
+  const T *xr = x + row * static_cast<int64_t>(K);
+  const int nvec = K >> 3;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int j = t + i * stride;
+    if (j < nvec) v[i] = ld_stream_v4(xr + static_cast<int64_t>(j) * 8);
+  }
+}
+
+template <typename T, int VPL, int WPR>
+__device__ __forceinline__ void pipe_row(const uint4 (&v)[VPL], uint8_t *xq, float *scale,
+                                         int64_t row, int K, int t, int stride, int group,
+                                         int parity, uint32_t (*redu)[WPR], float (*redf)[WPR]) {
+  const int nvec = K >> 3;
+  const int lane = t & 31, wi = t >> 5;
+  uint32_t mb = 0;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+    if (t + i * stride < nvec) mb = mag_max8(mb, v[i]);
+  mb = __reduce_max_sync(0xffffffffu, fold_halves(mb));
+  if constexpr (WPR > 1) {
+    uint32_t *slot = redu[2 * group + parity];
+    if (lane == 0) slot[wi] = mb;
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(32 * WPR) : "memory");
+#pragma unroll
+    for (int w = 0; w < WPR; ++w) mb = mb > slot[w] ? mb : slot[w];
+  }
+  const bool finite = mb <= Bits<T>::kMaxFinite;  // group-uniform
+  float amax;
+  if (finite) {
+    amax = Bits<T>::to_float(mb);
+  } else {
+    amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+      if (t + i * stride < nvec) amax = amax8_float<T>(amax, v[i]);
+    amax = warp_max(amax);
+    if constexpr (WPR > 1) {
+      float *slot = redf[2 * group + parity];
+      if (lane == 0) slot[wi] = amax;
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(32 * WPR) : "memory");
+      amax = slot[0];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w) amax = fmaxf(amax, slot[w]);
+    }
+  }
+  const float sc = fmaxf(__fdiv_rn(amax, kE4M3Max), kScaleFloor);
+  const float inv = __fdiv_rn(1.0f, sc);
+  if (t == 0) scale[row] = sc;
+  uint8_t *qr = xq + row * static_cast<int64_t>(K);
+  // two loops behind one warp-uniform branch: a select between the two conversions
+  // inside one loop would evaluate both
+  if (finite) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int j = t + i * stride;
+      if (j < nvec)
+        *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) = quant8_fast<T>(v[i], inv);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int j = t + i * stride;
+      if (j < nvec)
+        *reinterpret_cast<uint2 *>(qr + static_cast<int64_t>(j) * 8) = quant8_clamp<T>(v[i], inv);
+    }
+  }
+}
+
+constexpr int kPipeThreads = 512;
+
+// Two row buffers in registers, written out as two explicit halves of the loop body.
+template <typename T, int VPL, int WPR>
+__global__ void __launch_bounds__(kPipeThreads)
+    quant_rows_pipe_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
+                           float *__restrict__ scale, int64_t M, int K, int trigger) {
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
+  // per group and row parity: one slot of WPR integer maxima and one of float maxima
+  __shared__ uint32_t redu[2 * (kPipeThreads / 32)][WPR];
+  __shared__ float redf[2 * (kPipeThreads / 32)][WPR];
+  const int warp = threadIdx.x >> 5;
+  const int group = warp / WPR;
+  const int t = (warp % WPR) * 32 + (threadIdx.x & 31);
+  const int stride = 32 * WPR;
+  const int groups_per_cta = static_cast<int>(blockDim.x >> 5) / WPR;
+  const int64_t G = static_cast<int64_t>(gridDim.x) * groups_per_cta;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * groups_per_cta + group;
+  uint4 a[VPL], b[VPL];
+  pipe_load<T, VPL>(a, x, row, M, K, t, stride);
+  int parity = 0;
+  while (row < M) {
+    const int64_t r1 = row + G;
+    pipe_load<T, VPL>(b, x, r1, M, K, t, stride);
+    pipe_row<T, VPL, WPR>(a, xq, scale, row, K, t, stride, group, parity, redu, redf);
+    parity ^= 1;
+    if (r1 >= M) break;
+    const int64_t r2 = r1 + G;
+    pipe_load<T, VPL>(a, x, r2, M, K, t, stride);
+    pipe_row<T, VPL, WPR>(b, xq, scale, r1, K, t, stride, group, parity, redu, redf);
+    parity ^= 1;
+    row = r2;
+  }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// NB rows in flight per group through shared memory: each thread copies its own 16-byte
+// vectors of a row with cp.async into its slots (stage[slot][i][thread], so a warp's
+// copies and reads cover 512 contiguous bytes) and reads back only what it copied
+// itself, so the data needs no barrier, only the thread's own cp.async.wait_group. One
+// commit group per row (empty past M) keeps the group count uniform: after committing
+// row r + (NB - 1) G, waiting until NB - 1 groups remain pending means row r has landed.
+template <typename T, int VPL, int WPR, int NB>
+__global__ void __launch_bounds__(kPipeThreads)
+    quant_rows_pipe_async_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
+                                 float *__restrict__ scale, int64_t M, int K, int trigger) {
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
+  extern __shared__ __align__(16) uint4 stage[];  // [NB][VPL][blockDim.x]
+  __shared__ uint32_t redu[2 * (kPipeThreads / 32)][WPR];
+  __shared__ float redf[2 * (kPipeThreads / 32)][WPR];
+  const int warp = threadIdx.x >> 5;
+  const int group = warp / WPR;
+  const int t = (warp % WPR) * 32 + (threadIdx.x & 31);
+  const int stride = 32 * WPR;
+  const int nthr = static_cast<int>(blockDim.x);
+  const int nvec = K >> 3;
+  const int groups_per_cta = nthr / 32 / WPR;
+  const int64_t G = static_cast<int64_t>(gridDim.x) * groups_per_cta;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * groups_per_cta + group;
+  const uint32_t sbase = ptx::smem_u32(stage) + 16u * threadIdx.x;
+  auto issue = [&](int64_t r, int slot) {
+    if (r < M) {
+      const T *xr = x + r * static_cast<int64_t>(K);
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int j = t + i * stride;
+        if (j < nvec)
+          cp_async16(sbase + 16u * static_cast<uint32_t>((slot * VPL + i) * nthr),
+                     xr + static_cast<int64_t>(j) * 8);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int k = 0; k < NB - 1; ++k) issue(row0 + k * G, k);
+  int parity = 0, slot = 0;
+  for (int64_t r = row0; r < M; r += G) {
+    issue(r + (NB - 1) * G, slot == 0 ? NB - 1 : slot - 1);
+    cp_async_wait<NB - 1>();
+    uint4 v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+      if (t + i * stride < nvec) v[i] = stage[(slot * VPL + i) * nthr + threadIdx.x];
+    pipe_row<T, VPL, WPR>(v, xq, scale, r, K, t, stride, group, parity, redu, redf);
+    parity ^= 1;
+    slot = slot + 1 == NB ? 0 : slot + 1;
+  }
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------- streaming kernel
@@ -303,7 +502,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
     quant_rows_bulk_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
                            float *__restrict__ scale, int64_t M, int K, int nslot, int nwarps,
                            int trigger) {
-  if (trigger) ptx::grid_launch_dependents();
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   extern __shared__ __align__(128) uint8_t qsm[];
   const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;
   const uint32_t sbase = ptx::smem_u32(qsm);
@@ -401,7 +601,8 @@ __global__ void __launch_bounds__(256) quant_rows_generic_kernel(const T *__rest
                                                                  float *__restrict__ scale,
                                                                  int64_t M, int64_t K,
                                                                  int trigger) {
-  if (trigger) ptx::grid_launch_dependents();
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const T *xr = x + row * K;
@@ -502,6 +703,100 @@ cudaError_t launch_rows_bulk(const T *xp, int64_t M, int64_t K, uint8_t *xq, flo
   return cudaGetLastError();
 }
 
+// Launch as a programmatic dependent of the previous kernel on the stream: the grid may
+// be scheduled while that kernel finishes, and waits for it (griddepcontrol.wait, trigger
+// bit 1) before touching memory, so only the launch latency overlaps.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*k)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                             cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+// CTAs of `Kernel` one SM holds at a block size and dynamic shared memory, per device
+// (one cache per kernel instantiation; the first query also sets the kernel's dynamic
+// shared memory limit).
+template <auto Kernel>
+int blocks_per_sm(int device, int threads, size_t smem, cudaError_t *err) {
+  static std::mutex mu;
+  static int cache[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  int &c = cache[device & 63];
+  if (c == 0) {
+    *err = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem));
+    if (*err == cudaSuccess)
+      *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c, Kernel, threads, smem);
+    if (*err == cudaSuccess && c < 1) *err = cudaErrorInvalidConfiguration;
+    if (*err != cudaSuccess) c = 0;
+  }
+  return c;
+}
+
+constexpr int kPipeBlock = 256;                   // threads per CTA of the pipelined kernels
+constexpr int64_t kPipeRegMinBytes = 256ll << 20;  // register form from this input size up
+
+// Pipelined per-token quantizer for K % 8 == 0, K <= 16384 (16-byte aligned rows): a
+// persistent grid of every CTA the SMs hold (capped at one group per row). Inputs below
+// kPipeRegMinBytes stream through cp.async slots (two rows in flight per group), larger
+// ones through the two register buffers; both measured on B200 as the faster form at
+// their sizes.
+template <typename T, int VPL, int WPR>
+cudaError_t launch_rows_pipe(const T *xp, int64_t M, int64_t K, uint8_t *xq, float *scale,
+                             cudaStream_t stream, int trig, const DeviceInfo &dev) {
+  cudaError_t e = cudaSuccess;
+  const int gpc = kPipeBlock / 32 / WPR;
+  const int64_t need = (M + gpc - 1) / gpc;
+  if (M * K * 2 >= kPipeRegMinBytes) {
+    auto k = quant_rows_pipe_kernel<T, VPL, WPR>;
+    const int occ = blocks_per_sm<quant_rows_pipe_kernel<T, VPL, WPR>>(dev.device, kPipeBlock, 0, &e);
+    if (e != cudaSuccess) return e;
+    const int64_t grid = std::min<int64_t>(need, static_cast<int64_t>(occ) * dev.sm_count);
+    return launch_dependent(k, static_cast<unsigned>(grid), kPipeBlock, 0, stream, xp, xq, scale,
+                            M, static_cast<int>(K), trig);
+  }
+  auto k = quant_rows_pipe_async_kernel<T, VPL, WPR, 2>;
+  const size_t smem = static_cast<size_t>(2) * VPL * kPipeBlock * 16;
+  const int occ =
+      blocks_per_sm<quant_rows_pipe_async_kernel<T, VPL, WPR, 2>>(dev.device, kPipeBlock, smem, &e);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = std::min<int64_t>(need, static_cast<int64_t>(occ) * dev.sm_count);
+  return launch_dependent(k, static_cast<unsigned>(grid), kPipeBlock, smem, stream, xp, xq, scale,
+                          M, static_cast<int>(K), trig);
+}
+
+// Rows of nvec 16-byte vectors: twice the fewest warps per row that keep a thread at
+// <= 8 vectors (at most 8 warps), then the vectors per thread that covers the row.
+template <typename T>
+bool launch_rows_pipe_any(const T *xp, int64_t M, int64_t K, uint8_t *xq, float *scale,
+                          cudaStream_t stream, int trig, const DeviceInfo &dev, cudaError_t *e) {
+  const int64_t nvec = K / 8;
+  int wpr = 1;
+  while ((nvec + 32 * wpr - 1) / (32 * wpr) > 8 && wpr < 8) wpr *= 2;
+  wpr = wpr * 2 > 8 ? 8 : wpr * 2;
+  const int64_t per = (nvec + 32 * wpr - 1) / (32 * wpr);
+  if (per > 8) return false;
+  const int vpl = per <= 2 ? 2 : per <= 4 ? 4 : per <= 6 ? 6 : 8;
+#define FP8LIN_PIPE_CASE(V, W)                                                     \
+  if (vpl == V && wpr == W) {                                                       \
+    *e = launch_rows_pipe<T, V, W>(xp, M, K, xq, scale, stream, trig, dev);         \
+    return true;                                                                    \
+  }
+  FP8LIN_PIPE_CASE(2, 2) FP8LIN_PIPE_CASE(4, 2) FP8LIN_PIPE_CASE(2, 4) FP8LIN_PIPE_CASE(4, 4)
+  FP8LIN_PIPE_CASE(2, 8) FP8LIN_PIPE_CASE(4, 8) FP8LIN_PIPE_CASE(6, 8) FP8LIN_PIPE_CASE(8, 8)
+#undef FP8LIN_PIPE_CASE
+  return false;
+}
+
 template <typename T>
 cudaError_t launch_rows_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, float *scale,
                               cudaStream_t stream, bool trigger) {
@@ -510,11 +805,16 @@ cudaError_t launch_rows_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, 
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(xq) % 8 == 0);
   DeviceInfo dev;
-  // Streaming kernel for large inputs whose rows are whole multiples of 16 bytes and
-  // fit the ring twice; the register kernel below for the rest.
-  if (K % 8 == 0 && aligned && 2 * K * 2 <= static_cast<int64_t>(kBulkRing) &&
-      M * K * 2 >= kBulkMinBytes && current_device_info(&dev))
-    return launch_rows_bulk<T>(xp, M, K, xq, scale, stream, trigger, dev);
+  // 16-byte rows up to K = 16384: the pipelined kernels, launched as programmatic
+  // dependents; streaming kernel for larger inputs of wider rows that fit the ring
+  // twice; the register kernel below for the rest.
+  if (K % 8 == 0 && aligned && current_device_info(&dev)) {
+    cudaError_t e = cudaSuccess;
+    if (launch_rows_pipe_any<T>(xp, M, K, xq, scale, stream, (trigger ? 1 : 0) | 2, dev, &e))
+      return e;
+    if (2 * K * 2 <= static_cast<int64_t>(kBulkRing) && M * K * 2 >= kBulkMinBytes)
+      return launch_rows_bulk<T>(xp, M, K, xq, scale, stream, trigger, dev);
+  }
   int vpt = nvec >= 256 ? 8 : nvec >= 128 ? 4 : nvec >= 64 ? 2 : 1;
   int64_t tpr = ((nvec + vpt - 1) / vpt + 31) / 32 * 32;
   if (K % 8 == 0 && aligned && tpr <= 1024) {
@@ -951,12 +1251,18 @@ __global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
   const float inv = __fdiv_rn(1.0f, sc);
   if (lane == 0) xs[row] = sc;
   uint8_t *qr = xq + row * static_cast<int64_t>(K);
+  if (finite) {  // warp-uniform: one conversion per value, not both and a select
 #pragma unroll
-  for (int i = 0; i < CPL; ++i) {
-    const int c = lane + 32 * i;
-    if (c < nch)
-      *reinterpret_cast<uint2 *>(qr + 8 * c) =
-          finite ? quant8_fast<T>(v[i], inv) : quant8_clamp<T>(v[i], inv);
+    for (int i = 0; i < CPL; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nch) *reinterpret_cast<uint2 *>(qr + 8 * c) = quant8_fast<T>(v[i], inv);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nch) *reinterpret_cast<uint2 *>(qr + 8 * c) = quant8_clamp<T>(v[i], inv);
+    }
   }
 }
 

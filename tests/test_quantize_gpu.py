@@ -90,6 +90,34 @@ def test_quantize_edge_values(oracle):
         assert np.array_equal(u32(xs), osc.view(np.uint32)), dtype
 
 
+@pytest.mark.parametrize("M,K", [(3000, 1024), (3000, 3072), (2000, 12288), (1000, 15360),
+                                 (9000, 15360)])
+def test_quantize_nonfinite_rows_among_finite(M, K, oracle):
+    """Rows holding inf or NaN scattered among finite rows, at widths where a row spans 2,
+    4 or 8 warps (the per-row barrier exchange) and at sizes of both pipelined forms
+    (9000 x 15360 is above the register form's 256 MB threshold). Every non-finite row,
+    its neighbours and a sample of the rest are checked against the oracle."""
+    from fp8linear_b200 import ops
+
+    g = torch.Generator(device="cpu").manual_seed(M + K)
+    x = torch.randn(M, K, generator=g)
+    bad = torch.arange(5, M, 97)
+    x[bad, (bad * 31) % K] = float("inf")
+    x[bad[1::2], (bad[1::2] * 17) % K] = float("nan")
+    x[bad[::3], (bad[::3] * 13) % K] = float("-inf")
+    x[bad[-1]] = float("nan")  # an all-NaN row
+    x[bad[-2]] = 0.0           # and an all-zero row
+    x = x.bfloat16().cuda()
+    xq, xs = ops.quantize_fp8(x)
+    torch.cuda.synchronize()
+    rows = set(bad.tolist()) | set((bad + 1).clamp(max=M - 1).tolist()) | set(
+        (bad - 1).tolist()) | set(_rows(M, 256, seed=K).tolist())
+    sel = torch.tensor(sorted(rows), device="cuda")
+    oq, osc = oracle.c_quantize_rows(bits16(x[sel]), oracle.BF16)
+    assert np.array_equal(codes(xq[sel]), oq)
+    assert np.array_equal(u32(xs[sel]), osc.view(np.uint32))
+
+
 def test_quantize_empty_and_one_row():
     from fp8linear_b200 import ops
 
