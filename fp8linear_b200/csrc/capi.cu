@@ -177,7 +177,7 @@ int fp8lin_fp8_gemm(const void *xq, const float *x_scale, const void *wq, const 
   if (rc != FP8LIN_OK || M == 0 || N == 0) return rc;
   GemmArgs a{static_cast<const uint8_t *>(xq), x_scale, static_cast<const uint8_t *>(wq),
              w_scale, bias, bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
-  return launch_gemm(a, static_cast<cudaStream_t>(stream), false);
+  return launch_gemm(a, static_cast<cudaStream_t>(stream), true);
 }
 
 size_t fp8lin_linear_workspace_size(int64_t M, int64_t K) {
@@ -214,6 +214,7 @@ int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq, const float *w
                                      cudaGetErrorString(e));
   GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
              bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 
@@ -237,7 +238,7 @@ int fp8lin_mxfp8_gemm(const void *xq, const void *x_scales, const void *wq, cons
   a.mx = true;
   a.xsf = static_cast<const uint8_t *>(x_scales);
   a.wsf = static_cast<const uint8_t *>(w_scales);
-  return launch_gemm(a, static_cast<cudaStream_t>(stream), false);
+  return launch_gemm(a, static_cast<cudaStream_t>(stream), true);
 }
 
 size_t fp8lin_mxfp8_linear_workspace_size(int64_t M, int64_t K) {
@@ -281,6 +282,7 @@ int fp8lin_mxfp8_linear(const void *x, int x_dtype, const void *wq, const void *
   a.mx = true;
   a.xsf = xsf;
   a.wsf = static_cast<const uint8_t *>(w_scales);
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 
@@ -334,7 +336,7 @@ int fp8lin_nvfp4_gemm(const void *xq, const void *x_scales, const void *wq, cons
   a.nv = true;
   a.xsf = static_cast<const uint8_t *>(x_scales);
   a.wsf = static_cast<const uint8_t *>(w_scales);
-  return launch_gemm(a, static_cast<cudaStream_t>(stream), false);
+  return launch_gemm(a, static_cast<cudaStream_t>(stream), true);
 }
 
 size_t fp8lin_nvfp4_linear_workspace_size(int64_t M, int64_t K) {
@@ -379,6 +381,7 @@ int fp8lin_nvfp4_linear(const void *x, int x_dtype, const void *wq, const void *
   a.nv = true;
   a.xsf = xsf;
   a.wsf = static_cast<const uint8_t *>(w_scales);
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 
@@ -453,6 +456,7 @@ int fp8lin_fp8_linear_modulated(const void *x, int x_dtype, int64_t M, int64_t K
                                      cudaGetErrorString(e));
   GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
              bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 
@@ -578,6 +582,7 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
     // A ragged last chunk of a multi-chunk call takes the CTA-pair kernel like the full
     // chunks, so every row is summed in the order the whole-M call uses.
     a.pairs_only = chunks > 1;
+    a.weights_before_wait = true;  // the previous kernel is this chunk's quantizer
     rc = launch_gemm(a, h->comp, true);
     if (rc != FP8LIN_OK) break;  // launch_gemm set the message
     e = cudaEventRecord(h->comp_done[s], h->comp);
@@ -655,6 +660,7 @@ int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, cons
   a.ldo = ldo;
   a.n_peers = n_outs - 1;
   a.peers = outs + 1;
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 

@@ -232,6 +232,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // Everything above overlaps the previous kernel when launched as a PDL dependent;
   // nothing produced by it is read before this point.
   if (p.pdl) ptx::grid_dependency_wait();
+  // Everything before this kernel has completed: its dependents may launch (they wait for
+  // it in turn before touching memory).
+  ptx::grid_launch_dependents();
 
   const int num_tiles = p.m_tiles * p.n_tiles;
 

@@ -98,6 +98,7 @@ struct Params {
   uint32_t tmem_cols;
   uint32_t sf_col;   // block-scaled: TMEM column of the weight scales (token scales follow)
   int pdl;
+  int pre_w;         // weight boxes may be issued before the dependency wait
 };
 
 __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
@@ -161,10 +162,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ptx::mbar_init(bar_drain, 1);
     *abort = 0;
     ptx::fence_mbar_init();
-    // The weights do not depend on the kernel this one may overlap (PDL): start streaming
-    // them now. The first stages' weight boxes (and weight scale tiles) land in shared
-    // memory (each stage's barrier is armed for all its boxes; the token boxes follow after
-    // the dependency wait), the rest of this CTA's K-range is pulled into L2.
+  }
+  // The first stages' weight boxes (and weight scale tiles) go into shared memory at once
+  // (each stage's barrier armed for all its boxes; the token boxes follow in the producer
+  // loop), the rest of this CTA's K-range into L2. When the weights cannot depend on the
+  // kernel this one overlaps (pre_w: that kernel is this call's quantizer), this happens
+  // before the dependency wait, so the weight stream overlaps it.
+  auto issue_weights = [&]() {
     const int pre = nkb < STAGES ? nkb : STAGES;
     for (int i = 0; i < pre; ++i) {
       const uint32_t fb = bar_full + 8 * i;
@@ -175,7 +179,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
     }
     for (int i = pre; i < nkb; ++i) ptx::tma_prefetch_2d(&tmap_w, (kb0 + i) * BK, tile * WN);
-  }
+  };
+  if (threadIdx.x == 0 && p.pre_w) issue_weights();
   if (warp == 1) {
     ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t *>(tmem_slot)), p.tmem_cols);
     ptx::tmem_relinquish<1>();
@@ -185,6 +190,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (p.pdl) ptx::grid_dependency_wait();
+  // Everything before this kernel has completed: its dependents may launch (they wait for
+  // it in turn before touching memory).
+  ptx::grid_launch_dependents();
+  if (threadIdx.x == 0 && !p.pre_w) issue_weights();
+
+  // The reduction's operands that do not depend on the partials (x_scale of this block's
+  // tokens, w_scale and bias of the rows this CTA reduces), staged in shared memory by the
+  // epilogue warps while the main loop runs.
+  const int R = ((WN + p.split - 1) / p.split + 3) & ~3;
+  const int r0 = static_cast<int>(rank) * R;
+  const int r1 = min(WN, r0 + R);
+  const int quads = r1 > r0 ? (r1 - r0) >> 2 : 0;
+  float *e_xs = reinterpret_cast<float *>(smem + OFF_EPI);  // [MAX_TOK]
+  float *e_ws = e_xs + MAX_TOK;                              // [WN]: rows r0.. of the tile
+  float *e_b = e_ws + WN;
+  if (warp >= 2) {
+    const int et = threadIdx.x - 64;  // 0 .. 127
+    // block-scaled: the scales are inside the accumulator, out = fma(acc * 1, 1, bias)
+    for (int i = et; i < mrows; i += NUM_THREADS - 64)
+      e_xs[i] = C::BS ? 1.0f : __ldg(p.xs + tok0 + i);
+    for (int i = et; i < r1 - r0; i += NUM_THREADS - 64) {
+      const int n = tile * WN + r0 + i;
+      const bool in = n < p.N;
+      e_ws[i] = in ? (C::BS ? 1.0f : __ldg(p.ws + n)) : 0.0f;
+      e_b[i] = in && p.bias_dtype != kNone ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
+    }
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -298,25 +330,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 
   // CTA `rank` reduces tile rows [r0, r1) (a multiple of 4 wide) over the cluster's
-  // partials and writes out. Stage what that needs besides the partials first, so that
-  // its global-memory latency overlaps the cluster barrier.
-  const int R = ((WN + p.split - 1) / p.split + 3) & ~3;
-  const int r0 = static_cast<int>(rank) * R;
-  const int r1 = min(WN, r0 + R);
-  const int quads = r1 > r0 ? (r1 - r0) >> 2 : 0;
-  float *e_xs = reinterpret_cast<float *>(smem + OFF_EPI);  // [MAX_TOK]
-  float *e_ws = e_xs + MAX_TOK;                              // [WN]: rows r0.. of the tile
-  float *e_b = e_ws + WN;
-  // block-scaled: the scales are inside the accumulator, out = fma(acc * 1, 1, bias)
-  for (int i = threadIdx.x; i < mrows; i += NUM_THREADS)
-    e_xs[i] = C::BS ? 1.0f : __ldg(p.xs + tok0 + i);
-  for (int i = threadIdx.x; i < r1 - r0; i += NUM_THREADS) {
-    const int n = tile * WN + r0 + i;
-    const bool in = n < p.N;
-    e_ws[i] = in ? (C::BS ? 1.0f : __ldg(p.ws + n)) : 0.0f;
-    e_b[i] = in && p.bias_dtype != kNone ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
-  }
-
+  // partials and writes out.
   __syncwarp();
   __syncthreads();
   ptx::cluster_sync();  // every CTA's partial tile is in its shared memory
@@ -467,6 +481,7 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
   while (cols < used) cols <<= 1;
   p.tmem_cols = cols;
   p.pdl = pdl ? 1 : 0;
+  p.pre_w = pdl && a.weights_before_wait ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles * split, nblk);

@@ -91,11 +91,18 @@ struct GemmArgs {
   // Skip the few-token kernel and run CTA pairs at any M (same per-element summation
   // order as every larger M): the row chunks of one host-buffer call.
   bool pairs_only = false;
+  // The weights (and their scales) may be read before the programmatic dependency wait.
+  // Set only when the kernel launched just before on the stream is this library's
+  // quantizer of the same call: it lets its dependents launch only after its own wait
+  // has returned, so every kernel before it (a weight writer included) has completed.
+  bool weights_before_wait = false;
 };
 constexpr int kMaxPeers = 7;
 // Launches the tcgen05 GEMM + fused epilogue. `pdl` launches it as a programmatic
-// dependent of the previous kernel on the stream. Returns an fp8lin_status code and
-// sets the error message on failure.
+// dependent of the previous kernel on the stream: its set-up overlaps that kernel's tail
+// and it waits for it (griddepcontrol.wait) before reading activations or scales and
+// before writing anything. Returns an fp8lin_status code and sets the error message on
+// failure.
 int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl);
 // Reads (and optionally clears) the GEMM watchdog bits of the current device.
 cudaError_t read_gemm_status(unsigned int *bits, bool clear);
