@@ -47,6 +47,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "FP8 linear TFLOP/s at FLUX shapes vs 4.5 PF peak; quant GB/s vs 8 TB/s"
 FLUSH_BYTES = 256 << 20
+# idle time before each timed leg of a sweep: a bandwidth-bound kernel timed right after
+# tens of milliseconds of full-power GEMM replays reads up to 30 % slow
+SWEEP_PAUSE_S = 0.5
 NOMINAL_FP8_TFLOPS = 4500.0
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 L2_FALLBACK = 126 << 20
@@ -735,6 +738,7 @@ def measure_workload(name: str, steps: int, warmup: int, fmt: str = "fp8") -> di
     reps = max(steps, n_sets)
 
     def timed(call):
+        time.sleep(SWEEP_PAUSE_S)  # let the power state settle after the previous replays
         for i in range(warmup):
             call(sets[i % n_sets])
         g = graph_launches(call, sets, reps, keep=n_sets)
