@@ -931,15 +931,36 @@ __global__ void __launch_bounds__(32 * kMxWarps) quant_mx_kernel(
   }
   const int64_t sf_row = (row >> 7) * static_cast<int64_t>(ncb) * 512 + (row & 31) * 16 +
                          ((row & 127) >> 5) * 4;
+  // Magnitude maxima of this lane's 8-element groups with packed integer maxima (exact
+  // for finite and infinite values, which order like their bits); a maximum above the
+  // infinity pattern means the group holds a NaN. Segments without NaN (the normal
+  // case, warp-uniform) keep these maxima and convert with a multiply and the saturating
+  // convert: x * 2^(127 - e8) is below 512 for every finite x of a block, and an inf
+  // saturates to 448 exactly as the reference's clamp makes it. A segment with a NaN
+  // recomputes the maxima ignoring NaN and takes the literal clamp (NaN -> -448).
+  uint32_t m8[kMxVecs];
+  bool nan = false;
+#pragma unroll
+  for (int i = 0; i < kMxVecs; ++i) {
+    m8[i] = fold_halves(mag_max8(0u, v[i]));
+    nan |= m8[i] > MxBits<T>::kInf;
+  }
+  const bool any_nan = __any_sync(0xffffffffu, nan);
+  if (any_nan) {
+#pragma unroll
+    for (int i = 0; i < kMxVecs; ++i) m8[i] = mx_mag_max8<T>(v[i]);
+  }
+  float inv[kMxVecs];
 #pragma unroll
   for (int i = 0; i < kMxVecs; ++i) {
     const int el = e0 + (i * 32 + lane) * 8;
     const int g = el >> 5;  // this lane's block
     const bool live = row_live && g < nblk;
-    uint32_t mag = live ? mx_mag_max8<T>(v[i]) : 0u;
+    uint32_t mag = live ? m8[i] : 0u;
     mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 1));
     mag = max(mag, __shfl_xor_sync(0xffffffffu, mag, 2));
     const uint32_t e8 = live ? mx_block_e8<T>(mag) : 127u;
+    inv[i] = mx_inv(e8);
     // the scales of blocks g .. g+3 from lanes l, l+4, l+8, l+12 (l = 0, 16)
     const uint32_t b1 = __shfl_down_sync(0xffffffffu, e8, 4);
     const uint32_t b2 = __shfl_down_sync(0xffffffffu, e8, 8);
@@ -948,9 +969,21 @@ __global__ void __launch_bounds__(32 * kMxWarps) quant_mx_kernel(
     if ((lane & 15) == 0 && grp < ncb)
       *reinterpret_cast<uint32_t *>(sf + sf_row + static_cast<int64_t>(grp) * 512) =
           e8 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    if (live)
-      *reinterpret_cast<uint2 *>(xq + row * static_cast<int64_t>(K) + el) =
-          quant8_clamp<T>(v[i], mx_inv(e8));
+  }
+  uint8_t *qr = xq + row * static_cast<int64_t>(K);
+  // two loops behind the warp-uniform branch, so each value is converted once
+  if (!any_nan) {
+#pragma unroll
+    for (int i = 0; i < kMxVecs; ++i) {
+      const int el = e0 + (i * 32 + lane) * 8;
+      if (row_live && el < K) *reinterpret_cast<uint2 *>(qr + el) = quant8_fast<T>(v[i], inv[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kMxVecs; ++i) {
+      const int el = e0 + (i * 32 + lane) * 8;
+      if (row_live && el < K) *reinterpret_cast<uint2 *>(qr + el) = quant8_clamp<T>(v[i], inv[i]);
+    }
   }
 }
 

@@ -127,3 +127,26 @@ def test_nv_quantize_rejects_bad_k(capi):
         f.quantize_nvfp4(x)
     with pytest.raises(RuntimeError, match="multiple of 32"):
         capi.quantize_nvfp4(x)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_nv_quantize_nonfinite_segments_among_finite(oracle, dtype):
+    """inf and NaN in a few 1024-element segments of a 3000 x 3072 input (three segments
+    per row, several segments per warp of the persistent grid, the next one in flight):
+    segments with NaN take the literal clamp, the others the fast conversion, and both
+    must give the oracle's codes and scales for every row."""
+    import fp8linear_b200 as f
+
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x = torch.randn(3000, 3072, generator=g)
+    rows = torch.arange(3, 3000, 131)
+    x[rows, (rows * 37) % 3072] = float("nan")
+    x[rows[::2] + 1, (rows[::2] * 53) % 3072] = float("inf")
+    x[rows[1::3] + 2, (rows[1::3] * 7) % 3072] = float("-inf")
+    x[rows[-1]] = float("nan")
+    x = x.to(dtype).cuda()
+    xq, sc = f.quantize_nvfp4(x)
+    torch.cuda.synchronize()
+    oq, osc = oracle.np_quantize_nvfp4(bits16(x), oracle.BF16 if dtype == torch.bfloat16 else oracle.F16)
+    assert np.array_equal(sc.cpu().numpy(), osc)
+    assert np.array_equal(xq.cpu().numpy(), oq)
