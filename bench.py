@@ -492,7 +492,12 @@ def run_gpu(args):
                          "traffic": traffic,
                          "peak_basis": f"2 x {pk['source']} bf16 dense ({pk['bf16_tflops']} TFLOP/s)",
                          "frac_of_nominal_4p5pf": round(gemm_tflops / NOMINAL_FP8_TFLOPS, 4),
-                         "gemm_us": round(g_ms * 1e3, 2)},
+                         "gemm_us": round(g_ms * 1e3, 2),
+                         # launch time in SM cycles at the median sampled clock: equal
+                         # times at different clocks mean a bound outside the SM clock
+                         "gemm_sm_kcycles": (round(g_ms * clk["sm_mhz"], 1)
+                                             if clk.get("sm_mhz") else None),
+                         "sm_mhz_median": clk.get("sm_mhz")},
             "quantizer": {"achieved": round(quant_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                           "frac": round(quant_gbs / pk["hbm_gbs"], 4),
                           "us": round(q_ms * 1e3, 2), "bytes": wl.quant_bytes},
