@@ -1,5 +1,5 @@
 // ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the kernels use:
-// mbarriers, TMA (cp.async.bulk.tensor, never with .multicast::cluster), tcgen05
+// mbarriers, TMA (cp.async.bulk.tensor, never with cluster multicast), tcgen05
 // (TMEM alloc, MMA, commit, loads), programmatic dependent launch and the global
 // timer that bounds every wait.
 #pragma once
