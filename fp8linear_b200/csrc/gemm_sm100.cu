@@ -878,6 +878,28 @@ bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_
                             box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_128B, err);
 }
 
+bool make_tmap_chunks_u8(CUtensorMap *map, const void *base, uint64_t K, uint64_t rows,
+                         uint32_t box_rows, uint32_t box_chunks, std::string *err) {
+  auto fn = gemm::encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is unavailable (driver entry point query failed)";
+    return false;
+  }
+  cuuint64_t dims[3] = {128, rows, K / 128};
+  cuuint64_t strides[2] = {K, 128};
+  cuuint32_t box[3] = {128, box_rows, box_chunks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled (chunk view) failed with CUresult " +
+           std::to_string(static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
 // A tiled scale grid of `rows` rows as [row blocks][ncb tiles][128 words]; a box is
 // `tiles_per_box` consecutive tiles of one row block.
 bool make_tmap_sf(CUtensorMap *map, const void *base, uint64_t rows, uint64_t ncb,

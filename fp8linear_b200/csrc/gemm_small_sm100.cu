@@ -1,7 +1,8 @@
 // gemm_small_sm100.cu -- the FP8 GEMM + fused dequant/bias epilogue for few tokens
 // (M <= 128, and M <= 256 where it gets a K-split), where the work is streaming the weight
 // matrix once. Tokens go in blocks of 128 (grid y); each (weight tile, token block) pair
-// is one cluster.
+// is one cluster. Per-token e4m3 operands with at most 16 tokens go to the warp-level
+// kernel at the end of this file instead (whole weight rows per CTA, no cluster).
 //
 // Same result as fp8_gemm_kernel (out[m,n] = fma(acc * x_scale[m], w_scale[n], bias[n]),
 // acc = e4m3 dot products accumulated in fp32), organised for a weight-bandwidth-bound
@@ -167,20 +168,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // (each stage's barrier armed for all its boxes; the token boxes follow in the producer
   // loop), the rest of this CTA's K-range into L2. When the weights cannot depend on the
   // kernel this one overlaps (pre_w: that kernel is this call's quantizer), this happens
-  // before the dependency wait, so the weight stream overlaps it.
+  // before the dependency wait, so the weight stream overlaps it. Otherwise the whole
+  // K-range of the weight tile is prefetched into L2 before the wait (safe: writes of the
+  // kernel before land in the same L2 lines) and the first stages are loaded after it.
+  // (The first fill is unrolled over the compile-time ring, predicated on this CTA's
+  // K-blocks: issued from runtime loops, copies took about twice as long to go out.)
   auto issue_weights = [&]() {
-    const int pre = nkb < STAGES ? nkb : STAGES;
-    for (int i = 0; i < pre; ++i) {
-      const uint32_t fb = bar_full + 8 * i;
-      const uint32_t dst = sbase + static_cast<uint32_t>(i) * stage_bytes;
-      ptx::mbar_arrive_expect_tx(fb, stage_bytes);
-      ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
-      if constexpr (C::BS)
-        ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      if (i < nkb) {
+        const uint32_t fb = bar_full + 8 * i;
+        const uint32_t dst = sbase + static_cast<uint32_t>(i) * stage_bytes;
+        ptx::mbar_arrive_expect_tx(fb, stage_bytes);
+        ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
+        if constexpr (C::BS)
+          ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
+      }
     }
-    for (int i = pre; i < nkb; ++i) ptx::tma_prefetch_2d(&tmap_w, (kb0 + i) * BK, tile * WN);
   };
-  if (threadIdx.x == 0 && p.pre_w) issue_weights();
+  if (threadIdx.x == 0) {
+    if (p.pre_w) issue_weights();
+    for (int i = p.pre_w ? STAGES : 0; i < nkb; ++i)
+      ptx::tma_prefetch_2d(&tmap_w, (kb0 + i) * BK, tile * WN);
+  }
   if (warp == 1) {
     ptx::tmem_alloc<1>(ptx::smem_u32(const_cast<uint32_t *>(tmem_slot)), p.tmem_cols);
     ptx::tmem_relinquish<1>();
@@ -220,25 +230,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
+      // the first fill's token boxes (its stages are armed and their weight boxes issued)
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i) {
+        if (i < nkb) {
+          const uint32_t fb = bar_full + 8 * i;
+          const uint32_t dst = sbase + static_cast<uint32_t>(i) * stage_bytes;
+          ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, tok0, fb);
+          if constexpr (C::BS)
+            ptx::tma_load_3d(dst + sf_off + C::SF_STAGE, &tmap_xsf, 0, (kb0 + i) * C::SF_TILES,
+                             mb, fb);
+        }
+      }
+      int issued = nkb < STAGES ? nkb : STAGES;
+      // refills: a stage is rewritten once the MMAs reading it have completed
+      for (int i = STAGES; i < nkb; ++i) {
         const int s = i % STAGES;
         const uint32_t fb = bar_full + 8 * s;
         const uint32_t dst = sbase + static_cast<uint32_t>(s) * stage_bytes;
-        if (i >= STAGES) {
-          const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
-          if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kWaitLimitNs)) {
-            if (!*abort) {
-              atomicOr(&g_small_status, 16u);
-              *abort = 1;
-            }
-            break;
+        const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
+        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kWaitLimitNs)) {
+          if (!*abort) {
+            atomicOr(&g_small_status, 16u);
+            *abort = 1;
           }
-          ptx::mbar_arrive_expect_tx(fb, stage_bytes);
-          ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
-          if constexpr (C::BS)
-            ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
-        }  // else: armed and the weight boxes issued before the dependency wait
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(fb, stage_bytes);
+        ptx::tma_load_2d(dst, &tmap_w, (kb0 + i) * BK, tile * WN, fb);
+        if constexpr (C::BS)
+          ptx::tma_load_3d(dst + sf_off, &tmap_wsf, 0, (kb0 + i) * C::SF_TILES, tile, fb);
         ptx::tma_load_2d(dst + W_STAGE, &tmap_x, (kb0 + i) * BK, tok0, fb);
         if constexpr (C::BS)
           ptx::tma_load_3d(dst + sf_off + C::SF_STAGE, &tmap_xsf, 0, (kb0 + i) * C::SF_TILES, mb,
@@ -512,11 +533,407 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
 
 }  // namespace small
 
+// ---------------------------------------------------------------------------------------
+// At most 16 tokens (e4m3): warp-level MMAs over whole weight rows, no K-split across CTAs.
+//
+// With 16 or fewer tokens the 128-row tcgen05 tile spreads the weight matrix over the SMs
+// only by splitting K across a cluster, whose partial tiles then cross distributed shared
+// memory (~20 GB/s per SM) between two cluster barriers. Here a CTA owns 16 whole weight
+// rows (grid = ceil(N / 16), two CTAs per SM), so the weights still stream through every
+// SM and the only reduction is between the CTA's own warps:
+//  * warp 8 (one thread) streams K in stages of 1024 bytes through a ring of 3: per stage
+//    and operand one TMA copy of a chunk view of the matrix (8 chunks of 128 bytes x 16
+//    weight rows, or x 8 / 16 token rows; K % 128 == 0), else one 2-D box per chunk;
+//    128-byte swizzle; rows past N or M and bytes past K arrive as zeros. The ring's first
+//    fill is unrolled over its compile-time shape: issued from runtime loops, the copies
+//    took about twice as long to go out. The weight rows are also prefetched into L2
+//    before the dependency wait (L2 is where every SM's accesses meet, so this is safe
+//    even while the kernel before writes them);
+//  * warp w (0-7) takes chunk w of every stage: per 32-byte K-step one ldmatrix.x4 of the
+//    weights (rows 0-7 / 8-15 x bytes 0-15 / 16-31 of the step) and one ldmatrix of the
+//    tokens (8 tokens per fragment), the codes converted to f16 (exact) and summed by two
+//    mma.sync.m16n8k16 f16 x f16 -> f32 per 8 tokens (swap-AB: weight rows are the MMA's
+//    rows, tokens its columns), one accumulator set per K-step so the MMAs of a chunk do
+//    not wait for one another; the 128-byte swizzle puts the 8 rows of each ldmatrix in 8
+//    different bank groups;
+//  * the eight warps' fp32 partials meet in shared memory (over the consumed ring) and are
+//    summed in warp order (deterministic), then out = fma(acc * x_scale, w_scale, bias)
+//    as in the other kernels.
+// Waits are bounded as in the tcgen05 kernels (bit 16 of this file's watchdog word).
+namespace rows {
+
+constexpr int WR = 16;            // weight rows per CTA (the MMA's M)
+constexpr int CHUNK = 128;        // K-bytes per TMA box (one swizzled 128-byte row)
+constexpr int SC = 8;             // chunks per stage (1024 K-bytes)
+constexpr int CONSUMERS = 8;      // consumer warps, one per chunk (16 measured no faster)
+constexpr int KPW = (CHUNK / 32) * SC / CONSUMERS;  // K-steps per warp and stage (2)
+constexpr int STAGES = 3;
+constexpr int NUM_THREADS = 32 * (CONSUMERS + 1);
+constexpr int MAX_TOK = 16;
+constexpr uint32_t W_BOX = WR * CHUNK;                   // 2 KB
+constexpr uint32_t RED_BYTES = CONSUMERS * MAX_TOK * WR * 4;     // 16 KB, over the ring
+constexpr uint32_t PAR_BYTES = (MAX_TOK + 2 * WR) * 4;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint64_t kDrainLimitNs = 1000000000ull;
+
+// shared memory for `mpad` tokens per fragment set: [ring][params][barriers]; the warps'
+// partials overwrite the start of the ring once every stage has been consumed
+__host__ __device__ constexpr uint32_t stage_bytes(int mpad) {
+  return SC * (W_BOX + static_cast<uint32_t>(mpad) * CHUNK);
+}
+__host__ __device__ constexpr uint32_t off_par(int mpad) { return STAGES * stage_bytes(mpad); }
+__host__ __device__ constexpr uint32_t off_bar(int mpad) { return off_par(mpad) + PAR_BYTES; }
+__host__ __device__ constexpr uint32_t smem_bytes(int mpad) {
+  return off_bar(mpad) + 2 * STAGES * 8 + 8 + 1024;  // + abort word, base alignment slack
+}
+// two CTAs per SM (shared memory and, at <= 56 registers a thread, the register file)
+static_assert(2 * (smem_bytes(MAX_TOK) + 1024) <= 233472, "shared memory budget");
+static_assert(RED_BYTES <= STAGES * stage_bytes(8), "partials fit over the ring");
+static_assert(KPW * CONSUMERS == (CHUNK / 32) * SC, "K-steps split evenly");
+
+struct Params {
+  const uint8_t *wq;
+  const float *xs;
+  const float *ws;
+  const void *bias;
+  int bias_dtype;
+  void *out;
+  int out_dtype;
+  int M, N, K, ldo;
+  int chunks;   // ceil(K / 128)
+  int wide;     // maps are chunk views: one copy per stage and operand (K % 128 == 0)
+  int pdl;
+  int pre_w;    // weight boxes may be issued before the dependency wait
+};
+
+template <int MPAD>
+__global__ void __launch_bounds__(NUM_THREADS, 2)
+    fp8_gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                         const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+  constexpr uint32_t X_BOX = MPAD * CHUNK;
+  constexpr uint32_t STAGE = stage_bytes(MPAD);
+  constexpr int NT = MPAD / 8;  // 8-token fragments
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const uint32_t bar_full = sbase + off_bar(MPAD);
+  const uint32_t bar_empty = bar_full + 8 * STAGES;
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + off_bar(MPAD) + 16 * STAGES);
+  float *red = reinterpret_cast<float *>(smem);  // [warp][token][row], over the ring
+  float *e_xs = reinterpret_cast<float *>(smem + off_par(MPAD));  // [MAX_TOK]
+  float *e_ws = e_xs + MAX_TOK;                                   // [WR]
+  float *e_b = e_ws + WR;                                         // [WR]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * WR;
+  // The parameter fields the loops use, as locals: a lambda capturing the by-value
+  // parameter struct makes it addressable, and every read after a copy instruction (which
+  // clobbers memory) then went through a generic pointer into parameter space; that made
+  // issuing a copy cost ~0.1 us and tripled the time to put a CTA's stages in flight.
+  const int chunks = p.chunks;
+  const int nst = (chunks + SC - 1) / SC;
+  auto chunks_of = [chunks](int i) { return min(SC, chunks - i * SC); };
+
+  if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&tmap_w);
+    ptx::prefetch_tmap(&tmap_x);
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(bar_full + 8 * s, 1);
+      ptx::mbar_init(bar_empty + 8 * s, CONSUMERS);
+    }
+    *abort = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  // The first stages' weight boxes, armed for the whole stage (the token boxes follow
+  // after the dependency wait); before that wait only when the weights cannot depend on
+  // the kernel this one overlaps (pre_w: it is this call's quantizer).
+  // The ring's first fill is unrolled over its compile-time shape (STAGES x SC boxes,
+  // predicated on the real chunk count): issued from runtime loops the same copies took
+  // twice as long to put in flight.
+  // With chunk-view maps (wide) a stage is one copy per operand, and the box's chunks past
+  // K arrive as zeros (the consumers skip them); otherwise one 2-D box per chunk.
+  const bool wide = p.wide != 0;
+  auto stage_tx = [&](int i) {
+    return static_cast<uint32_t>(wide ? SC : chunks_of(i)) * (W_BOX + X_BOX);
+  };
+  auto load_w = [&](int i, uint32_t dst, uint32_t fb) {
+    if (wide) {
+      ptx::tma_load_3d(dst, &tmap_w, 0, n0, i * SC, fb);
+    } else {
+      const int cnt = chunks_of(i);
+#pragma unroll
+      for (int c = 0; c < SC; ++c)
+        if (c < cnt) ptx::tma_load_2d(dst + c * W_BOX, &tmap_w, (i * SC + c) * CHUNK, n0, fb);
+    }
+  };
+  auto load_x = [&](int i, uint32_t dst, uint32_t fb) {
+    if (wide) {
+      ptx::tma_load_3d(dst + SC * W_BOX, &tmap_x, 0, 0, i * SC, fb);
+    } else {
+      const int cnt = chunks_of(i);
+#pragma unroll
+      for (int c = 0; c < SC; ++c)
+        if (c < cnt)
+          ptx::tma_load_2d(dst + SC * W_BOX + c * X_BOX, &tmap_x, (i * SC + c) * CHUNK, 0, fb);
+    }
+  };
+  auto issue_weights = [&]() {
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      if (i < nst) {
+        const uint32_t fb = bar_full + 8 * i;
+        ptx::mbar_arrive_expect_tx(fb, stage_tx(i));
+        load_w(i, sbase + static_cast<uint32_t>(i) * STAGE, fb);
+      }
+    }
+  };
+  if (threadIdx.x == 32 * CONSUMERS) {
+    // this CTA's weight rows (contiguous) into L2 whatever the launch mode, so the weight
+    // stream overlaps the kernel before this one; then, under pre_w, the first stages
+    ptx::bulk_prefetch_l2(p.wq + static_cast<int64_t>(n0) * p.K,
+                          static_cast<uint32_t>(min(WR, p.N - n0)) * static_cast<uint32_t>(p.K));
+    if (p.pre_w) issue_weights();
+  }
+  if (p.pdl) ptx::grid_dependency_wait();
+  ptx::grid_launch_dependents();
+
+  if (warp == CONSUMERS) {
+    if (lane == 0) {
+      if (!p.pre_w) issue_weights();
+      // the first fill's token boxes (its stages are armed and their weight boxes issued)
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i)
+        if (i < nst) load_x(i, sbase + static_cast<uint32_t>(i) * STAGE, bar_full + 8 * i);
+      int issued = nst < STAGES ? nst : STAGES;
+      // refills: a stage is rewritten once its consumer warps have released it
+      for (int i = STAGES; i < nst; ++i) {
+        const int s = i % STAGES;
+        const uint32_t fb = bar_full + 8 * s;
+        const uint32_t dst = sbase + static_cast<uint32_t>(s) * STAGE;
+        const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
+        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1u, abort, kWaitLimitNs)) {
+          if (!*abort) {
+            atomicOr(&g_small_status, 16u);
+            *abort = 1;
+          }
+          break;
+        }
+        ptx::mbar_arrive_expect_tx(fb, stage_tx(i));
+        load_w(i, dst, fb);
+        load_x(i, dst, fb);
+        ++issued;
+      }
+      // no copy may still be landing when the CTA exits: wait for the last stages' data
+      // (the loop stops early only at i >= STAGES, so every armed stage was issued)
+      for (int i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
+        ptx::mbar_wait_timeout(bar_full + 8 * (i % STAGES),
+                               static_cast<uint32_t>(i / STAGES) & 1u, kDrainLimitNs);
+    }
+  } else {
+    // the epilogue's operands, loaded while the first stages land
+    if (warp == 0 && lane < WR) {
+      const int n = n0 + lane;
+      const bool in = n < p.N;
+      e_ws[lane] = in ? __ldg(p.ws + n) : 0.0f;
+      e_b[lane] = in && p.bias_dtype != kNone ? small::load_bias(p.bias, p.bias_dtype, n) : 0.0f;
+    } else if (warp == 1 && lane < MAX_TOK) {
+      e_xs[lane] = lane < p.M ? __ldg(p.xs + lane) : 0.0f;
+    }
+    // Warp w takes chunk w % SC of every stage, K-steps [k0, k0 + KS) of it, with one
+    // accumulator set per K-step so its MMAs do not wait for one another (a chained
+    // mma.sync costs its full latency per step).
+    constexpr int KS = KPW;
+    const int cw = warp % SC;
+    const int k0 = (warp / SC) * KS;
+    float acc[KS][NT][4];
+#pragma unroll
+    for (int k = 0; k < KS; ++k)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) acc[k][j][0] = acc[k][j][1] = acc[k][j][2] = acc[k][j][3] = 0.0f;
+    // ldmatrix row addresses (lane 8j + i: row i of matrix j), 16-byte chunk index before
+    // the swizzle: A matrices (rows 0-7 | 8-15) x (bytes 0-15 | 16-31) of a K-step; B
+    // matrices (bytes 0-15 | 16-31) x (tokens 0-7 | 8-15).
+    const int li = lane & 7, lj = lane >> 3;
+    const uint32_t a_row = static_cast<uint32_t>(li + (lj & 1) * 8) * CHUNK;
+    const int a_half = lj >> 1;
+    const uint32_t b_row = static_cast<uint32_t>(li + (NT == 2 ? (lj >> 1) * 8 : 0)) * CHUNK;
+    const int b_half = lj & 1;
+    for (int i = 0; i < nst; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
+      // one lane per warp polls the barrier (every thread polling it slowed the copies'
+      // arrival about twofold); the warp barrier then orders the other lanes' reads after
+      // that lane's acquire
+      int ok = 1;
+      if (lane == 0) ok = ptx::mbar_wait_bounded(bar_full + 8 * s, ph, abort, kWaitLimitNs);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      __syncwarp();
+      if (!ok) {
+        if (lane == 0 && !*abort) {
+          atomicOr(&g_small_status, 16u);
+          *abort = 1;
+        }
+        break;
+      }
+      if (cw < chunks_of(i)) {
+        const uint32_t wbox = sbase + static_cast<uint32_t>(s) * STAGE + cw * W_BOX;
+        const uint32_t xbox = sbase + static_cast<uint32_t>(s) * STAGE + SC * W_BOX + cw * X_BOX;
+        uint32_t a[KS][4], b[KS][4];
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          const int step = k0 + ks;
+          ptx::ldsm_x4(wbox + a_row + (static_cast<uint32_t>((2 * step + a_half) ^ li) << 4), a[ks]);
+          const uint32_t baddr = xbox + b_row + (static_cast<uint32_t>((2 * step + b_half) ^ li) << 4);
+          if constexpr (NT == 2)
+            ptx::ldsm_x4(baddr, b[ks]);
+          else
+            ptx::ldsm_x2(baddr, b[ks][0], b[ks][1]);
+        }
+        // Each 32-byte K-step as two f16 m16n8k16 MMAs (the codes convert to f16 exactly;
+        // the e4m3 form of the warp-level MMA ran several times slower here). Lane 4g + t
+        // holds bytes [4t, 4t + 4) of each 16-byte half; the MMA's K-slots (2t, 2t + 1) take
+        // bytes (4t, 4t + 1) and slots (2t + 8, 2t + 9) bytes (4t + 2, 4t + 3), for weights
+        // and tokens alike, so each MMA sums over exactly one half's 16 bytes.
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+          uint32_t af[8];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            af[4 * h + 0] = ptx::e4m3x2_to_f16x2(a[ks][2 * h], 0);
+            af[4 * h + 1] = ptx::e4m3x2_to_f16x2(a[ks][2 * h + 1], 0);
+            af[4 * h + 2] = ptx::e4m3x2_to_f16x2(a[ks][2 * h], 1);
+            af[4 * h + 3] = ptx::e4m3x2_to_f16x2(a[ks][2 * h + 1], 1);
+          }
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t bv = b[ks][2 * j + h];
+              ptx::mma_f16_16x8x16(acc[ks][j], af[4 * h], af[4 * h + 1], af[4 * h + 2],
+                                   af[4 * h + 3], ptx::e4m3x2_to_f16x2(bv, 0),
+                                   ptx::e4m3x2_to_f16x2(bv, 1));
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
+    }
+    // this warp's partial [tokens][rows]: the K-step accumulators summed in order
+#pragma unroll
+    for (int k = 1; k < KS; ++k)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[0][j][e] += acc[k][j][e];
+    // every consumer warp is past its last stage (and every stage it waited on has
+    // landed), so the partials may overwrite the ring; the producer warp only waits on
+    // barriers from here on
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * CONSUMERS) : "memory");
+    const int g = lane >> 2, t = lane & 3;
+    float *r = red + warp * (MAX_TOK * WR);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int tok = 8 * j + 2 * t;
+      r[tok * WR + g] = acc[0][j][0];
+      r[(tok + 1) * WR + g] = acc[0][j][1];
+      r[tok * WR + g + 8] = acc[0][j][2];
+      r[(tok + 1) * WR + g + 8] = acc[0][j][3];
+    }
+  }
+  __syncwarp();
+  __syncthreads();
+  if (*abort) return;
+  for (int idx = threadIdx.x; idx < p.M * WR; idx += NUM_THREADS) {
+    const int tok = idx / WR, row = idx - tok * WR;
+    const int n = n0 + row;
+    if (n >= p.N) continue;
+    float sum = red[tok * WR + row];
+#pragma unroll
+    for (int w = 1; w < CONSUMERS; ++w) sum += red[w * (MAX_TOK * WR) + tok * WR + row];
+    const float val = fmaf(sum * e_xs[tok], e_ws[row], e_b[row]);
+    const int64_t o = static_cast<int64_t>(tok) * p.ldo + n;
+    if (p.out_dtype == kF16)
+      reinterpret_cast<__half *>(p.out)[o] = __float2half_rn(val);
+    else
+      reinterpret_cast<__nv_bfloat16 *>(p.out)[o] = __float2bfloat16_rn(val);
+  }
+}
+
+template <int MPAD>
+int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
+  std::string err;
+  CUtensorMap tw, tx;
+  // chunk views (one copy per stage and operand) when K allows; 2-D boxes otherwise
+  bool wide = a.K % CHUNK == 0 && make_tmap_chunks_u8(&tw, a.wq, a.K, a.N, WR, SC, &err) &&
+              make_tmap_chunks_u8(&tx, a.xq, a.K, a.M, MPAD, SC, &err);
+  if (!wide && (!make_tmap_2d_u8(&tw, a.wq, a.K, a.N, CHUNK, WR, &err) ||
+                !make_tmap_2d_u8(&tx, a.xq, a.K, a.M, CHUNK, MPAD, &err))) {
+    set_error("fp8_gemm: " + err);
+    return 4;
+  }
+  static std::once_flag once[64];
+  static cudaError_t setup_err[64];
+  const int d = dev.device & 63;
+  std::call_once(once[d], [&] {
+    setup_err[d] = cudaFuncSetAttribute(fp8_gemm_rows_kernel<MPAD>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem_bytes(MPAD)));
+  });
+  if (setup_err[d] != cudaSuccess) {
+    set_error(std::string("fp8_gemm: rows kernel setup: ") + cudaGetErrorString(setup_err[d]));
+    return 4;
+  }
+  Params p;
+  p.wq = a.wq;
+  p.xs = a.xs;
+  p.ws = a.ws;
+  p.bias = a.bias;
+  p.bias_dtype = a.bias ? a.bias_dtype : kNone;
+  p.out = a.out;
+  p.out_dtype = a.out_dtype;
+  p.M = static_cast<int>(a.M);
+  p.N = static_cast<int>(a.N);
+  p.K = static_cast<int>(a.K);
+  p.ldo = static_cast<int>(a.ldo > 0 ? a.ldo : a.N);
+  p.chunks = static_cast<int>((a.K + CHUNK - 1) / CHUNK);
+  p.wide = wide ? 1 : 0;
+  p.pdl = pdl ? 1 : 0;
+  p.pre_w = pdl && a.weights_before_wait ? 1 : 0;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((a.N + WR - 1) / WR));
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = smem_bytes(MPAD);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_rows_kernel<MPAD>, tw, tx, p);
+  if (ce != cudaSuccess) {
+    set_error(std::string("fp8_gemm: rows kernel launch failed: ") + cudaGetErrorString(ce));
+    return 4;
+  }
+  return 0;
+}
+
+}  // namespace rows
+
 int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   DeviceInfo dev;
   if (!current_device_info(&dev)) return 5;
   if (a.nv) return small::launch<small::kFmtNV>(a, dev, stream, pdl);
   if (a.mx) return small::launch<small::kFmtMX>(a, dev, stream, pdl);
+  if (a.M <= 8) return rows::launch<8>(a, dev, stream, pdl);
+  if (a.M <= rows::MAX_TOK) return rows::launch<16>(a, dev, stream, pdl);
   return small::launch<small::kFmtE4M3>(a, dev, stream, pdl);
 }
 

@@ -123,5 +123,12 @@ cudaError_t read_small_status(unsigned int *bits, bool clear);
 // 2-D uint8 tensor map with 128-byte swizzle (shared by both GEMM shapes).
 bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
                      uint32_t box_inner, uint32_t box_outer, std::string *err);
+// A row-major uint8 [rows, K] matrix (K % 128 == 0) viewed as (128 bytes, row, 128-byte
+// chunk): a box of `box_rows` rows x `box_chunks` chunks lands as [chunk][row][128 B], each
+// chunk's rows 128-byte swizzled, i.e. the same shared-memory image as that many 2-D boxes
+// of 128 bytes x `box_rows` rows, in one copy. Every coordinate inside its extent addresses
+// inside the matrix.
+bool make_tmap_chunks_u8(CUtensorMap *map, const void *base, uint64_t K, uint64_t rows,
+                         uint32_t box_rows, uint32_t box_chunks, std::string *err);
 
 }  // namespace fp8lin

@@ -1,7 +1,8 @@
 // ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the kernels use:
 // mbarriers, TMA (cp.async.bulk.tensor, never with cluster multicast), tcgen05
-// (TMEM alloc, MMA, commit, loads), programmatic dependent launch and the global
-// timer that bounds every wait.
+// (TMEM alloc, MMA, commit, loads), programmatic dependent launch, the global timer that
+// bounds every wait, and the warp-level f16 MMA (with ldmatrix and the exact e4m3 -> f16
+// conversion) of the kernel for at most 16 tokens.
 #pragma once
 
 #include <cstdint>
@@ -124,6 +125,16 @@ __device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int32_t x, int
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
                    reinterpret_cast<uint64_t>(tmap)),
                "r"(x), "r"(y)
+               : "memory");
+}
+
+// Brings `bytes` contiguous bytes at `src` into L2 (address 16-byte aligned, size a
+// multiple of 16). L2 is where every SM's accesses to device memory meet, so a prefetch
+// issued before a programmatic dependency wait is safe even for data the previous kernel
+// is still writing: those writes update the L2 lines, and reads after the wait see them.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
                : "memory");
 }
 
@@ -539,6 +550,47 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// ---------------------------------------------------------------- warp-level MMA
+
+// Four 8 x 16-byte matrices from shared memory: lane 8j + i gives the address of row i of
+// matrix j (16-byte aligned); register j of lane 4g + t receives bytes [4t, 4t + 4) of row
+// g of matrix j.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+// Two matrices (addresses from lanes 0-15).
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr)
+               : "memory");
+}
+
+// Two e4m3 codes (bytes 0-1 or 2-3 of `v`) as an f16x2 pair, exactly (every e4m3 value
+// is an f16 value); the lower byte lands in the lower half.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v, int hi) {
+  uint32_t r;
+  const uint16_t pair = static_cast<uint16_t>(hi ? (v >> 16) : (v & 0xFFFFu));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(pair));
+  return r;
+}
+
+// d (16 x 8, f32) += a (16 x 16, f16, row-major) * b (16 x 8, f16, column-major). Lane
+// 4g + t holds a = {row g k 2t.., row g+8 k 2t.., row g k 2t+8.., row g+8 k 2t+8..},
+// b = {col g k 2t.., col g k 2t+8..} (2 values per register) and d as below.
+__device__ __forceinline__ void mma_f16_16x8x16(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                uint32_t a2, uint32_t a3, uint32_t b0,
+                                                uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 }  // namespace ptx
