@@ -54,7 +54,10 @@ def _oracle_out(oracle, xq, xs, wq, ws, b):
      (256, 1024, 1024), (1000, 3072, 3072), (64, 9216, 3072), (513, 776, 4096),
      (255, 512, 12288), (3, 1, 16), (64, 44, 1024), (200, 100, 512), (257, 1003, 256),
      (333, 384, 1024), (1000, 640, 512), (192, 3072, 3072), (256, 9216, 3072),
-     (384, 1024, 3072), (500, 2048, 2048)],
+     (384, 1024, 3072), (500, 2048, 2048),
+     # 64 < M <= 128 on the few-token kernel: narrow and wide N, ragged token rows, long K
+     (65, 3072, 3072), (96, 1000, 2080), (128, 9216, 3072), (100, 21504, 3072),
+     (128, 3072, 15360), (127, 136, 256)],
 )
 def test_gemm_shapes_vs_oracle(M, N, K, oracle):
     from fp8linear_b200 import ops
