@@ -566,12 +566,12 @@ constexpr int WR = 16;            // weight rows per CTA (the MMA's M)
 constexpr int CHUNK = 128;        // K-bytes per TMA box (one swizzled 128-byte row)
 constexpr int SC = 8;             // chunks per stage (1024 K-bytes)
 constexpr int CONSUMERS = 8;      // consumer warps, one per chunk (16 measured no faster)
-constexpr int KPW = (CHUNK / 32) * SC / CONSUMERS;  // K-steps per warp and stage (2)
+constexpr int KPW = (CHUNK / 32) * SC / CONSUMERS;  // K-steps per warp and stage (4)
 constexpr int STAGES = 3;
 constexpr int NUM_THREADS = 32 * (CONSUMERS + 1);
 constexpr int MAX_TOK = 16;
 constexpr uint32_t W_BOX = WR * CHUNK;                   // 2 KB
-constexpr uint32_t RED_BYTES = CONSUMERS * MAX_TOK * WR * 4;     // 16 KB, over the ring
+constexpr uint32_t RED_BYTES = CONSUMERS * MAX_TOK * WR * 4;     // 8 KB, over the ring
 constexpr uint32_t PAR_BYTES = (MAX_TOK + 2 * WR) * 4;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint64_t kDrainLimitNs = 1000000000ull;
@@ -586,7 +586,7 @@ __host__ __device__ constexpr uint32_t off_bar(int mpad) { return off_par(mpad) 
 __host__ __device__ constexpr uint32_t smem_bytes(int mpad) {
   return off_bar(mpad) + 2 * STAGES * 8 + 8 + 1024;  // + abort word, base alignment slack
 }
-// two CTAs per SM (shared memory and, at <= 56 registers a thread, the register file)
+// two CTAs per SM (shared memory here; registers through the launch bounds)
 static_assert(2 * (smem_bytes(MAX_TOK) + 1024) <= 233472, "shared memory budget");
 static_assert(RED_BYTES <= STAGES * stage_bytes(8), "partials fit over the ring");
 static_assert(KPW * CONSUMERS == (CHUNK / 32) * SC, "K-steps split evenly");
@@ -627,10 +627,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * WR;
-  // The parameter fields the loops use, as locals: a lambda capturing the by-value
-  // parameter struct makes it addressable, and every read after a copy instruction (which
-  // clobbers memory) then went through a generic pointer into parameter space; that made
-  // issuing a copy cost ~0.1 us and tripled the time to put a CTA's stages in flight.
+  // 128-byte chunks of K and stages (the last ones may be partial)
   const int chunks = p.chunks;
   const int nst = (chunks + SC - 1) / SC;
   auto chunks_of = [chunks](int i) { return min(SC, chunks - i * SC); };
@@ -646,14 +643,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     ptx::fence_mbar_init();
   }
   __syncthreads();
-  // The first stages' weight boxes, armed for the whole stage (the token boxes follow
-  // after the dependency wait); before that wait only when the weights cannot depend on
-  // the kernel this one overlaps (pre_w: it is this call's quantizer).
-  // The ring's first fill is unrolled over its compile-time shape (STAGES x SC boxes,
-  // predicated on the real chunk count): issued from runtime loops the same copies took
-  // twice as long to put in flight.
-  // With chunk-view maps (wide) a stage is one copy per operand, and the box's chunks past
-  // K arrive as zeros (the consumers skip them); otherwise one 2-D box per chunk.
+  // The first stages' weight copies, each stage armed for all its bytes (the token copies
+  // follow after the dependency wait); before that wait only when the weights cannot
+  // depend on the kernel this one overlaps (pre_w: it is this call's quantizer). The first
+  // fill is unrolled over the compile-time ring, predicated on the real chunk count:
+  // issued from runtime loops the same copies took twice as long to go out. With
+  // chunk-view maps (wide) a stage is one copy per operand, the box's chunks past K
+  // arriving as zeros (the consumers skip them); otherwise one 2-D box per chunk.
   const bool wide = p.wide != 0;
   auto stage_tx = [&](int i) {
     return static_cast<uint32_t>(wide ? SC : chunks_of(i)) * (W_BOX + X_BOX);
@@ -763,9 +759,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     for (int i = 0; i < nst; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = static_cast<uint32_t>(i / STAGES) & 1u;
-      // one lane per warp polls the barrier (every thread polling it slowed the copies'
-      // arrival about twofold); the warp barrier then orders the other lanes' reads after
-      // that lane's acquire
+      // one lane per warp polls the barrier; the warp barrier then orders the other
+      // lanes' reads after that lane's acquire
       int ok = 1;
       if (lane == 0) ok = ptx::mbar_wait_bounded(bar_full + 8 * s, ph, abort, kWaitLimitNs);
       ok = __shfl_sync(0xffffffffu, ok, 0);
