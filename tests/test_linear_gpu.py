@@ -99,3 +99,36 @@ def test_quantize_and_fp8linear_module():
     assert out.dtype == torch.bfloat16 and out.shape == (4, 33, 128)
     rel = float((out.float() - ref_out).norm() / ref_out.norm())
     assert rel < 0.1
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 300])
+def test_fp8_linear_right_after_the_weight_writer(M):
+    """quantize_weight writes the codes and the fused linear follows on the stream with no
+    synchronization between them. The per-token quantizer lets the GEMM launch before its
+    own dependency wait, and the GEMM prefetches its weights into L2 before its wait, so
+    the prefetch can overlap the writer; every read after the wait must still see the new
+    codes. Each round rewrites the same weight buffers with other values (the warp-level
+    kernel, the split-K kernel and the CTA pairs); the outputs must equal the ones computed
+    after a full synchronize, bit for bit."""
+    import fp8linear_b200 as f
+    from fp8linear_b200 import ops
+
+    g = torch.Generator(device="cpu").manual_seed(M)
+    x = torch.randn(M, 3072, generator=g).bfloat16().cuda()
+    ws_list = [(torch.randn(3072, 3072, generator=g) * 0.02).bfloat16().cuda() for _ in range(4)]
+    b = (torch.randn(3072, generator=g) * 0.02).bfloat16().cuda()
+    wq = torch.empty(3072, 3072, dtype=torch.float8_e4m3fn, device="cuda")
+    wsc = torch.empty(3072, dtype=torch.float32, device="cuda")
+    outs = []
+    for w in ws_list:  # writer, then the linear, back to back
+        q, s = ops.quantize_weight(w)
+        wq.copy_(q)
+        wsc.copy_(s)
+        outs.append(f.fp8_linear(x, wq, wsc, b))
+    torch.cuda.synchronize()
+    for w, got in zip(ws_list, outs):
+        q, s = ops.quantize_weight(w)
+        torch.cuda.synchronize()
+        ref = f.fp8_linear(x, q, s, b)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref)
