@@ -214,6 +214,7 @@ int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq, const float *w
                                      cudaGetErrorString(e));
   GemmArgs a{xq, xs, static_cast<const uint8_t *>(wq), w_scale, bias,
              bias ? bias_dtype : kNone, out, out_dtype, M, N, K};
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 
@@ -581,7 +582,8 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
     // A ragged last chunk of a multi-chunk call takes the CTA-pair kernel like the full
     // chunks, so every row is summed in the order the whole-M call uses.
     a.pairs_only = chunks > 1;
-      rc = launch_gemm(a, h->comp, true);
+    a.weights_before_wait = true;  // the previous kernel is this chunk's quantizer
+    rc = launch_gemm(a, h->comp, true);
     if (rc != FP8LIN_OK) break;  // launch_gemm set the message
     e = cudaEventRecord(h->comp_done[s], h->comp);
     // download chunk i
@@ -658,6 +660,7 @@ int fp8lin_fp8_linear_allgather(const void *x, int x_dtype, const void *wq, cons
   a.ldo = ldo;
   a.n_peers = n_outs - 1;
   a.peers = outs + 1;
+  a.weights_before_wait = true;  // the previous kernel is this call's quantizer
   return launch_gemm(a, s, true);
 }
 

@@ -92,11 +92,9 @@ struct GemmArgs {
   // order as every larger M): the row chunks of one host-buffer call.
   bool pairs_only = false;
   // The weights (and their scales) may be read before the programmatic dependency wait.
-  // Set only when the kernel launched just before on the stream is this library's MXFP8,
-  // NVFP4 or LayerNorm-modulation quantizer of the same call: a plain launch, so every
-  // kernel before it (a weight writer included) has completed when it lets its dependents
-  // go. Not behind the per-token quantizer, which lets its dependents launch before its
-  // own dependency wait (the GEMM then only prefetches its weights into L2 early).
+  // Set only when the kernel launched just before on the stream is this library's
+  // quantizer of the same call: it lets its dependents launch only after its own wait
+  // has returned, so every kernel before it (a weight writer included) has completed.
   bool weights_before_wait = false;
 };
 constexpr int kMaxPeers = 7;

@@ -205,13 +205,9 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const T *__restric
                                                               int64_t M, int K, int tpr,
                                                               int trigger) {
   // trigger bit 0: let the dependent grid launch now; bit 1: this grid is itself a
-  // programmatic dependent and waits for its prerequisite before touching memory. The
-  // dependents are let go first: a grid launches its dependents only once all of its own
-  // CTAs are running, so a dependent that waits in turn can starve no one, and the GEMM
-  // behind this quantizer reads nothing before its own wait but prefetches its weights
-  // into L2, overlapping the kernel before this one.
-  if (trigger & 1) ptx::grid_launch_dependents();
+  // programmatic dependent and waits for its prerequisite before touching memory
   if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   __shared__ uint32_t red[32];
   const int t_in_row = threadIdx.x % tpr;
   const int row_in_cta = threadIdx.x / tpr;
@@ -386,8 +382,8 @@ template <typename T, int VPL, int WPR>
 __global__ void __launch_bounds__(kPipeThreads)
     quant_rows_pipe_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
                            float *__restrict__ scale, int64_t M, int K, int trigger) {
-  if (trigger & 1) ptx::grid_launch_dependents();
   if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   // per group and row parity: one slot of WPR integer maxima and one of float maxima
   __shared__ uint32_t redu[2 * (kPipeThreads / 32)][WPR];
   __shared__ float redf[2 * (kPipeThreads / 32)][WPR];
@@ -436,8 +432,8 @@ template <typename T, int VPL, int WPR, int NB>
 __global__ void __launch_bounds__(kPipeThreads)
     quant_rows_pipe_async_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
                                  float *__restrict__ scale, int64_t M, int K, int trigger) {
-  if (trigger & 1) ptx::grid_launch_dependents();
   if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   extern __shared__ __align__(16) uint4 stage[];  // [NB][VPL][blockDim.x]
   __shared__ uint32_t redu[2 * (kPipeThreads / 32)][WPR];
   __shared__ float redf[2 * (kPipeThreads / 32)][WPR];
@@ -506,8 +502,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1)
     quant_rows_bulk_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
                            float *__restrict__ scale, int64_t M, int K, int nslot, int nwarps,
                            int trigger) {
-  if (trigger & 1) ptx::grid_launch_dependents();
   if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   extern __shared__ __align__(128) uint8_t qsm[];
   const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;
   const uint32_t sbase = ptx::smem_u32(qsm);
@@ -605,8 +601,8 @@ __global__ void __launch_bounds__(256) quant_rows_generic_kernel(const T *__rest
                                                                  float *__restrict__ scale,
                                                                  int64_t M, int64_t K,
                                                                  int trigger) {
-  if (trigger & 1) ptx::grid_launch_dependents();
   if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const T *xr = x + row * K;

@@ -103,13 +103,14 @@ def test_quantize_and_fp8linear_module():
 
 @pytest.mark.parametrize("M", [1, 16, 64, 300])
 def test_fp8_linear_right_after_the_weight_writer(M):
-    """quantize_weight writes the codes and the fused linear follows on the stream with no
-    synchronization between them. The per-token quantizer lets the GEMM launch before its
-    own dependency wait, and the GEMM prefetches its weights into L2 before its wait, so
-    the prefetch can overlap the writer; every read after the wait must still see the new
-    codes. Each round rewrites the same weight buffers with other values (the warp-level
-    kernel, the split-K kernel and the CTA pairs); the outputs must equal the ones computed
-    after a full synchronize, bit for bit."""
+    """The weight buffers are rewritten and the fused linear follows on the stream with no
+    synchronization between them. Behind this library's per-token quantizer the
+    few-token GEMMs load their first weight stages before their own dependency wait (the
+    quantizer lets them launch only after its wait, so after the writer has completed),
+    and they prefetch their weights into L2 early; every read must see the new codes. Each
+    round rewrites the same buffers with other values (the warp-level kernel, the split-K
+    kernel and the CTA pairs); the outputs must equal the ones computed after a full
+    synchronize, bit for bit."""
     import fp8linear_b200 as f
     from fp8linear_b200 import ops
 
