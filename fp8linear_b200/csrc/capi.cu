@@ -208,7 +208,14 @@ int fp8lin_fp8_linear(const void *x, int x_dtype, const void *wq, const float *w
   float *xs = reinterpret_cast<float *>(
       xq + round_up(static_cast<size_t>(M) * static_cast<size_t>(K), kWsAlign));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_quantize_rows(x, x_dtype, M, K, xq, xs, s, true);
+  // Few tokens (the GEMM streams the weight matrix once): the quantizer, which launches
+  // while the kernel before it still runs, brings the weights into L2 on the way.
+  L2Prefetch pf;
+  if (M <= kFewTokenMaxM) {
+    pf.ptr = wq;
+    pf.bytes = N * K;
+  }
+  cudaError_t e = launch_quantize_rows(x, x_dtype, M, K, xq, xs, s, true, pf);
   if (e != cudaSuccess)
     return fail(FP8LIN_ERR_CUDA, std::string("fp8_linear: quantize launch: ") +
                                      cudaGetErrorString(e));

@@ -929,7 +929,7 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
       set_error("block-scaled gemm: peer outputs are not supported");
       return 2;
     }
-    if (a.M <= 2 * gemm::BM && !a.pairs_only) {
+    if (a.M <= kFewTokenMaxM && !a.pairs_only) {
       const int rc = launch_gemm_small(a, stream, pdl);
       if (rc != kSmallDeclined) return rc;
     }
@@ -939,7 +939,7 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   // Few tokens: stream the weights with swap-AB split-K tiles (M <= 128; up to 256 where
   // the kernel gets a K-split). Otherwise CTA pairs with 256-row tiles (or single CTAs
   // with 128-row tiles for peer outputs at M <= 128).
-  if (a.M <= 2 * gemm::BM && a.n_peers == 0 && !a.pairs_only) {
+  if (a.M <= kFewTokenMaxM && a.n_peers == 0 && !a.pairs_only) {
     const int rc = launch_gemm_small(a, stream, pdl);
     if (rc != kSmallDeclined) return rc;
   }

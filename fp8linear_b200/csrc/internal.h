@@ -30,9 +30,18 @@ struct DeviceInfo {
 bool current_device_info(DeviceInfo *info);
 
 // ---- quantize.cu
+// A device range to bring into L2 (16-byte aligned start, size a multiple of 16).
+struct L2Prefetch {
+  const void *ptr = nullptr;
+  int64_t bytes = 0;
+};
 // Per-token quantization (activation path). Returns cudaSuccess or the launch error.
+// `prefetch`: the range the kernel launched next reads (a fused linear's weights), which
+// the quantizer's CTAs bring into L2 before their dependency wait, i.e. while the kernel
+// before still runs (the pipelined form only; the grid widens so each CTA takes ~64 KB).
 cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
-                                 float *scale, cudaStream_t stream, bool trigger_dependents);
+                                 float *scale, cudaStream_t stream, bool trigger_dependents,
+                                 const L2Prefetch &prefetch = {});
 // MXFP8 block quantization (per 32 elements along K, e8m0 scales in the tiled
 // block-scale layout; the whole padded scale grid of mx_scale_bytes(M, K) is written).
 // K % 32 == 0, x 16-byte aligned, xq 8-byte aligned, scales 4-byte aligned.
@@ -98,6 +107,8 @@ struct GemmArgs {
   bool weights_before_wait = false;
 };
 constexpr int kMaxPeers = 7;
+// Token counts up to which the GEMM may run a few-token kernel (it streams the weights once).
+constexpr int64_t kFewTokenMaxM = 256;
 // Launches the tcgen05 GEMM + fused epilogue. `pdl` launches it as a programmatic
 // dependent of the previous kernel on the stream: its set-up overlaps that kernel's tail
 // and it waits for it (griddepcontrol.wait) before reading activations or scales and

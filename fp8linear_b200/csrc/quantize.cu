@@ -428,10 +428,21 @@ __device__ __forceinline__ void cp_async_wait() {
 // itself, so the data needs no barrier, only the thread's own cp.async.wait_group. One
 // commit group per row (empty past M) keeps the group count uniform: after committing
 // row r + (NB - 1) G, waiting until NB - 1 groups remain pending means row r has landed.
+// `pf` / `pf_bytes`: a range the kernel launched after this one will read (the fused
+// linear's weight matrix), brought into L2 before this grid's own dependency wait, one
+// slice per CTA; L2 is where every SM's accesses to device memory meet, so this is safe
+// even while the kernel before still writes the range.
 template <typename T, int VPL, int WPR, int NB>
 __global__ void __launch_bounds__(kPipeThreads)
     quant_rows_pipe_async_kernel(const T *__restrict__ x, uint8_t *__restrict__ xq,
-                                 float *__restrict__ scale, int64_t M, int K, int trigger) {
+                                 float *__restrict__ scale, int64_t M, int K, int trigger,
+                                 const uint8_t *pf, int64_t pf_bytes) {
+  if (pf_bytes > 0 && threadIdx.x == 0) {
+    const int64_t slice = ((pf_bytes + gridDim.x - 1) / gridDim.x + 15) & ~int64_t{15};
+    const int64_t off = static_cast<int64_t>(blockIdx.x) * slice;
+    if (off < pf_bytes)
+      ptx::bulk_prefetch_l2(pf + off, static_cast<uint32_t>(min(slice, pf_bytes - off)));
+  }
   if (trigger & 2) ptx::grid_dependency_wait();
   if (trigger & 1) ptx::grid_launch_dependents();
   extern __shared__ __align__(16) uint4 stage[];  // [NB][VPL][blockDim.x]
@@ -752,7 +763,8 @@ constexpr int64_t kPipeRegMinBytes = 256ll << 20;  // register form from this in
 // their sizes.
 template <typename T, int VPL, int WPR>
 cudaError_t launch_rows_pipe(const T *xp, int64_t M, int64_t K, uint8_t *xq, float *scale,
-                             cudaStream_t stream, int trig, const DeviceInfo &dev) {
+                             cudaStream_t stream, int trig, const DeviceInfo &dev,
+                             const L2Prefetch &pf) {
   cudaError_t e = cudaSuccess;
   const int gpc = kPipeBlock / 32 / WPR;
   const int64_t need = (M + gpc - 1) / gpc;
@@ -769,16 +781,22 @@ cudaError_t launch_rows_pipe(const T *xp, int64_t M, int64_t K, uint8_t *xq, flo
   const int occ =
       blocks_per_sm<quant_rows_pipe_async_kernel<T, VPL, WPR, 2>>(dev.device, kPipeBlock, smem, &e);
   if (e != cudaSuccess) return e;
-  const int64_t grid = std::min<int64_t>(need, static_cast<int64_t>(occ) * dev.sm_count);
+  const int64_t resident = static_cast<int64_t>(occ) * dev.sm_count;
+  int64_t grid = std::min<int64_t>(need, resident);
+  // with a prefetch, enough CTAs (rowless ones only prefetch) for ~64 KB slices
+  if (pf.bytes > 0) grid = std::max(grid, std::min<int64_t>(resident, (pf.bytes + 65535) / 65536));
   return launch_dependent(k, static_cast<unsigned>(grid), kPipeBlock, smem, stream, xp, xq, scale,
-                          M, static_cast<int>(K), trig);
+                          M, static_cast<int>(K), trig,
+                          static_cast<const uint8_t *>(pf.bytes > 0 ? pf.ptr : nullptr),
+                          pf.bytes > 0 ? pf.bytes : int64_t{0});
 }
 
 // Rows of nvec 16-byte vectors: twice the fewest warps per row that keep a thread at
 // <= 8 vectors (at most 8 warps), then the vectors per thread that covers the row.
 template <typename T>
 bool launch_rows_pipe_any(const T *xp, int64_t M, int64_t K, uint8_t *xq, float *scale,
-                          cudaStream_t stream, int trig, const DeviceInfo &dev, cudaError_t *e) {
+                          cudaStream_t stream, int trig, const DeviceInfo &dev, cudaError_t *e,
+                          const L2Prefetch &pf) {
   const int64_t nvec = K / 8;
   int wpr = 1;
   while ((nvec + 32 * wpr - 1) / (32 * wpr) > 8 && wpr < 8) wpr *= 2;
@@ -788,7 +806,7 @@ bool launch_rows_pipe_any(const T *xp, int64_t M, int64_t K, uint8_t *xq, float 
   const int vpl = per <= 2 ? 2 : per <= 4 ? 4 : per <= 6 ? 6 : 8;
 #define FP8LIN_PIPE_CASE(V, W)                                                     \
   if (vpl == V && wpr == W) {                                                       \
-    *e = launch_rows_pipe<T, V, W>(xp, M, K, xq, scale, stream, trig, dev);         \
+    *e = launch_rows_pipe<T, V, W>(xp, M, K, xq, scale, stream, trig, dev, pf);     \
     return true;                                                                    \
   }
   FP8LIN_PIPE_CASE(2, 2) FP8LIN_PIPE_CASE(4, 2) FP8LIN_PIPE_CASE(2, 4) FP8LIN_PIPE_CASE(4, 4)
@@ -799,7 +817,7 @@ bool launch_rows_pipe_any(const T *xp, int64_t M, int64_t K, uint8_t *xq, float 
 
 template <typename T>
 cudaError_t launch_rows_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, float *scale,
-                              cudaStream_t stream, bool trigger) {
+                              cudaStream_t stream, bool trigger, const L2Prefetch &pf) {
   const T *xp = reinterpret_cast<const T *>(x);
   const int64_t nvec = K / 8;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
@@ -810,7 +828,7 @@ cudaError_t launch_rows_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, 
   // twice; the register kernel below for the rest.
   if (K % 8 == 0 && aligned && current_device_info(&dev)) {
     cudaError_t e = cudaSuccess;
-    if (launch_rows_pipe_any<T>(xp, M, K, xq, scale, stream, (trigger ? 1 : 0) | 2, dev, &e))
+    if (launch_rows_pipe_any<T>(xp, M, K, xq, scale, stream, (trigger ? 1 : 0) | 2, dev, &e, pf))
       return e;
     if (2 * K * 2 <= static_cast<int64_t>(kBulkRing) && M * K * 2 >= kBulkMinBytes)
       return launch_rows_bulk<T>(xp, M, K, xq, scale, stream, trigger, dev);
@@ -1332,11 +1350,13 @@ cudaError_t launch_ln_typed(const void *x, const void *shift, const void *scale,
 }  // namespace
 
 cudaError_t launch_quantize_rows(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
-                                 float *scale, cudaStream_t stream, bool trigger_dependents) {
+                                 float *scale, cudaStream_t stream, bool trigger_dependents,
+                                 const L2Prefetch &prefetch) {
   if (M == 0) return cudaSuccess;
   if (dtype == kBF16)
-    return launch_rows_typed<__nv_bfloat16>(x, M, K, xq, scale, stream, trigger_dependents);
-  return launch_rows_typed<__half>(x, M, K, xq, scale, stream, trigger_dependents);
+    return launch_rows_typed<__nv_bfloat16>(x, M, K, xq, scale, stream, trigger_dependents,
+                                            prefetch);
+  return launch_rows_typed<__half>(x, M, K, xq, scale, stream, trigger_dependents, prefetch);
 }
 
 cudaError_t launch_quantize_mx(const void *x, int dtype, int64_t M, int64_t K, uint8_t *xq,
