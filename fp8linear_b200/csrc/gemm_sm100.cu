@@ -908,6 +908,14 @@ bool make_tmap_sf(CUtensorMap *map, const void *base, uint64_t rows, uint64_t nc
                             (rows + 127) / 128, 512, ncb * 512, 128, tiles_per_box, err);
 }
 
+// The same grid with a box of `box_words` 32-bit words of `tiles_per_box` consecutive tiles
+// of one row block (box_words 64: one half of each tile, 32 rows' scale lines).
+bool make_tmap_sf_box(CUtensorMap *map, const void *base, uint64_t rows, uint64_t ncb,
+                      uint32_t box_words, uint32_t tiles_per_box, std::string *err) {
+  return gemm::make_tmap_3d(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, base, 128, ncb,
+                            (rows + 127) / 128, 512, ncb * 512, box_words, tiles_per_box, err);
+}
+
 int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   if (a.M == 0 || a.N == 0) return 0;
   DeviceInfo dev;

@@ -1,8 +1,9 @@
 // gemm_small_sm100.cu -- the FP8 GEMM + fused dequant/bias epilogue for few tokens
 // (M <= 128, and M <= 256 where it gets a K-split), where the work is streaming the weight
 // matrix once. Tokens go in blocks of 128 (grid y); each (weight tile, token block) pair
-// is one cluster. Per-token e4m3 operands with at most 16 tokens go to the warp-level
-// kernel at the end of this file instead (whole weight rows per CTA, no cluster).
+// is one cluster. Per-token e4m3 operands with at most 16 tokens, and MXFP8 with at most 8
+// (K % 128 == 0), go to the warp-level kernel at the end of this file instead (whole
+// weight rows per CTA, no cluster).
 //
 // Same result as fp8_gemm_kernel (out[m,n] = fma(acc * x_scale[m], w_scale[n], bias[n]),
 // acc = e4m3 dot products accumulated in fp32), organised for a weight-bandwidth-bound
@@ -403,6 +404,8 @@ bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_
                      uint32_t box_inner, uint32_t box_outer, std::string *err);
 bool make_tmap_sf(CUtensorMap *map, const void *base, uint64_t rows, uint64_t ncb,
                   uint32_t tiles_per_box, std::string *err);
+bool make_tmap_sf_box(CUtensorMap *map, const void *base, uint64_t rows, uint64_t ncb,
+                      uint32_t box_words, uint32_t tiles_per_box, std::string *err);
 
 namespace small {
 
@@ -559,6 +562,11 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
 //  * the eight warps' fp32 partials meet in shared memory (over the consumed ring) and are
 //    summed in warp order (deterministic), then out = fma(acc * x_scale, w_scale, bias)
 //    as in the other kernels.
+// MXFP8 form (F = kFmtMX, at most 8 tokens, K % 128 == 0): a stage also carries, per
+// operand, one 3-D copy of the 256-byte halves of its 8 scale tiles that hold the CTA's
+// rows (a chunk is one tile column of 4 blocks). A 32-byte K-step is one 32-element block:
+// its two MMAs sum into a zeroed temporary, which joins the accumulator as
+// (sum * 2^(ea - 127)) * 2^(eb - 127) with the weight row's and the token's e8m0 scales.
 // Waits are bounded as in the tcgen05 kernels (bit 16 of this file's watchdog word).
 namespace rows {
 
@@ -576,19 +584,33 @@ constexpr uint32_t PAR_BYTES = (MAX_TOK + 2 * WR) * 4;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint64_t kDrainLimitNs = 1000000000ull;
 
-// shared memory for `mpad` tokens per fragment set: [ring][params][barriers]; the warps'
-// partials overwrite the start of the ring once every stage has been consumed
-__host__ __device__ constexpr uint32_t stage_bytes(int mpad) {
-  return SC * (W_BOX + static_cast<uint32_t>(mpad) * CHUNK);
+// MXFP8: per stage and operand the 256-byte halves of the stage's 8 scale tiles that hold
+// the CTA's 16 rows (a tile holds 128 rows x 4 blocks of 32; a chunk is one tile column)
+constexpr uint32_t SF_WIN = SC * 256;
+
+// shared memory for `mpad` tokens per fragment set: [ring][params][barriers]; a stage is
+// [weight boxes][token boxes][MX: weight and token scale windows]; the warps' partials
+// overwrite the start of the ring once every stage has been consumed
+__host__ __device__ constexpr uint32_t stage_bytes(int mpad, bool mx) {
+  return SC * (W_BOX + static_cast<uint32_t>(mpad) * CHUNK) + (mx ? 2 * SF_WIN : 0u);
 }
-__host__ __device__ constexpr uint32_t off_par(int mpad) { return STAGES * stage_bytes(mpad); }
-__host__ __device__ constexpr uint32_t off_bar(int mpad) { return off_par(mpad) + PAR_BYTES; }
-__host__ __device__ constexpr uint32_t smem_bytes(int mpad) {
-  return off_bar(mpad) + 2 * STAGES * 8 + 8 + 1024;  // + abort word, base alignment slack
+__host__ __device__ constexpr uint32_t off_par(int mpad, bool mx) {
+  return STAGES * stage_bytes(mpad, mx);
+}
+__host__ __device__ constexpr uint32_t off_bar(int mpad, bool mx) {
+  return off_par(mpad, mx) + PAR_BYTES;
+}
+__host__ __device__ constexpr uint32_t smem_bytes(int mpad, bool mx) {
+  return off_bar(mpad, mx) + 2 * STAGES * 8 + 8 + 1024;  // + abort word, alignment slack
 }
 // two CTAs per SM (shared memory here; registers through the launch bounds)
-static_assert(2 * (smem_bytes(MAX_TOK) + 1024) <= 233472, "shared memory budget");
-static_assert(RED_BYTES <= STAGES * stage_bytes(8), "partials fit over the ring");
+static_assert(2 * (smem_bytes(MAX_TOK, true) + 1024) <= 233472, "shared memory budget");
+static_assert(RED_BYTES <= STAGES * stage_bytes(8, false), "partials fit over the ring");
+
+// an e8m0 scale as a float: 2^(e - 127) (e = 0: 2^-127, a subnormal)
+__device__ __forceinline__ float e8m0_to_float(uint32_t e) {
+  return __uint_as_float(e ? e << 23 : 0x00400000u);
+}
 static_assert(KPW * CONSUMERS == (CHUNK / 32) * SC, "K-steps split evenly");
 
 struct Params {
@@ -606,22 +628,26 @@ struct Params {
   int pre_w;    // weight boxes may be issued before the dependency wait
 };
 
-template <int MPAD>
+template <int MPAD, int F>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     fp8_gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                         const __grid_constant__ CUtensorMap tmap_x, const Params p) {
+                         const __grid_constant__ CUtensorMap tmap_x,
+                         const __grid_constant__ CUtensorMap tmap_wsf,
+                         const __grid_constant__ CUtensorMap tmap_xsf, const Params p) {
+  constexpr bool MX = F == small::kFmtMX;
   constexpr uint32_t X_BOX = MPAD * CHUNK;
-  constexpr uint32_t STAGE = stage_bytes(MPAD);
+  constexpr uint32_t STAGE = stage_bytes(MPAD, MX);
+  constexpr uint32_t SF_OFF = SC * (W_BOX + X_BOX);  // MX: weight window; token window next
   constexpr int NT = MPAD / 8;  // 8-token fragments
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = ptx::smem_u32(smem);
-  const uint32_t bar_full = sbase + off_bar(MPAD);
+  const uint32_t bar_full = sbase + off_bar(MPAD, MX);
   const uint32_t bar_empty = bar_full + 8 * STAGES;
-  volatile int *abort = reinterpret_cast<volatile int *>(smem + off_bar(MPAD) + 16 * STAGES);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + off_bar(MPAD, MX) + 16 * STAGES);
   float *red = reinterpret_cast<float *>(smem);  // [warp][token][row], over the ring
-  float *e_xs = reinterpret_cast<float *>(smem + off_par(MPAD));  // [MAX_TOK]
+  float *e_xs = reinterpret_cast<float *>(smem + off_par(MPAD, MX));  // [MAX_TOK]
   float *e_ws = e_xs + MAX_TOK;                                   // [WR]
   float *e_b = e_ws + WR;                                         // [WR]
 
@@ -632,9 +658,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const int nst = (chunks + SC - 1) / SC;
   auto chunks_of = [chunks](int i) { return min(SC, chunks - i * SC); };
 
+  // MX: the CTA's rows sit in half h of their scale tiles, as 32-row group q
+  const int sf_h = (n0 >> 4) & 1, sf_q = (n0 & 127) >> 5;
   if (threadIdx.x == 0) {
     ptx::prefetch_tmap(&tmap_w);
     ptx::prefetch_tmap(&tmap_x);
+    if constexpr (MX) {
+      ptx::prefetch_tmap(&tmap_wsf);
+      ptx::prefetch_tmap(&tmap_xsf);
+    }
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
       ptx::mbar_init(bar_empty + 8 * s, CONSUMERS);
@@ -652,11 +684,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   // arriving as zeros (the consumers skip them); otherwise one 2-D box per chunk.
   const bool wide = p.wide != 0;
   auto stage_tx = [&](int i) {
-    return static_cast<uint32_t>(wide ? SC : chunks_of(i)) * (W_BOX + X_BOX);
+    return static_cast<uint32_t>(wide ? SC : chunks_of(i)) * (W_BOX + X_BOX) +
+           (MX ? 2 * SF_WIN : 0u);
   };
+  // (MX runs with chunk views only: the host requires K % 128 == 0)
   auto load_w = [&](int i, uint32_t dst, uint32_t fb) {
     if (wide) {
       ptx::tma_load_3d(dst, &tmap_w, 0, n0, i * SC, fb);
+      if constexpr (MX) ptx::tma_load_3d(dst + SF_OFF, &tmap_wsf, sf_h * 64, i * SC, n0 >> 7, fb);
     } else {
       const int cnt = chunks_of(i);
 #pragma unroll
@@ -667,6 +702,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   auto load_x = [&](int i, uint32_t dst, uint32_t fb) {
     if (wide) {
       ptx::tma_load_3d(dst + SC * W_BOX, &tmap_x, 0, 0, i * SC, fb);
+      if constexpr (MX) ptx::tma_load_3d(dst + SF_OFF + SF_WIN, &tmap_xsf, 0, i * SC, 0, fb);
     } else {
       const int cnt = chunks_of(i);
 #pragma unroll
@@ -729,13 +765,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     }
   } else {
     // the epilogue's operands, loaded while the first stages land
+    // (MX: the scales are inside the accumulator, out = fma(acc * 1, 1, bias))
     if (warp == 0 && lane < WR) {
       const int n = n0 + lane;
       const bool in = n < p.N;
-      e_ws[lane] = in ? __ldg(p.ws + n) : 0.0f;
+      e_ws[lane] = in ? (MX ? 1.0f : __ldg(p.ws + n)) : 0.0f;
       e_b[lane] = in && p.bias_dtype != kNone ? small::load_bias(p.bias, p.bias_dtype, n) : 0.0f;
     } else if (warp == 1 && lane < MAX_TOK) {
-      e_xs[lane] = lane < p.M ? __ldg(p.xs + lane) : 0.0f;
+      e_xs[lane] = lane < p.M ? (MX ? 1.0f : __ldg(p.xs + lane)) : 0.0f;
     }
     // Warp w takes chunk w % SC of every stage, K-steps [k0, k0 + KS) of it, with one
     // accumulator set per K-step so its MMAs do not wait for one another (a chained
@@ -776,6 +813,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const uint32_t wbox = sbase + static_cast<uint32_t>(s) * STAGE + cw * W_BOX;
         const uint32_t xbox = sbase + static_cast<uint32_t>(s) * STAGE + SC * W_BOX + cw * X_BOX;
         uint32_t a[KS][4], b[KS][4];
+        // MX: the 4 block scales of this chunk for weight rows g, g + 8 and the lane's
+        // tokens, one 32-bit word each (a row's scales of one tile are 4 consecutive bytes)
+        uint32_t sw0 = 0, sw1 = 0, sx[NT][2] = {};
+        if constexpr (MX) {
+          const int g = lane >> 2, t = lane & 3;
+          const uint8_t *sfw = smem + s * STAGE + SF_OFF + cw * 256 + sf_q * 4;
+          const uint8_t *sfx = smem + s * STAGE + SF_OFF + SF_WIN + cw * 256;
+          sw0 = *reinterpret_cast<const uint32_t *>(sfw + g * 16);
+          sw1 = *reinterpret_cast<const uint32_t *>(sfw + (g + 8) * 16);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            sx[j][0] = *reinterpret_cast<const uint32_t *>(sfx + (8 * j + 2 * t) * 16);
+            sx[j][1] = *reinterpret_cast<const uint32_t *>(sfx + (8 * j + 2 * t + 1) * 16);
+          }
+        }
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           const int step = k0 + ks;
@@ -801,14 +853,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             af[4 * h + 2] = ptx::e4m3x2_to_f16x2(a[ks][2 * h], 1);
             af[4 * h + 3] = ptx::e4m3x2_to_f16x2(a[ks][2 * h + 1], 1);
           }
+          if constexpr (MX) {
+            // the step is one 32-element block: its sum, scaled by the weight row's and
+            // the token's 2^(e - 127), joins the accumulator ((sum * sa) * sb: a zero sum
+            // stays zero whatever the scales); byte `step` of each scale word
+            const int sh = 8 * (k0 + ks);
+            const float sa0 = e8m0_to_float((sw0 >> sh) & 0xFFu);
+            const float sa1 = e8m0_to_float((sw1 >> sh) & 0xFFu);
 #pragma unroll
-          for (int j = 0; j < NT; ++j) {
+            for (int j = 0; j < NT; ++j) {
+              float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t bv = b[ks][2 * j + h];
-              ptx::mma_f16_16x8x16(acc[ks][j], af[4 * h], af[4 * h + 1], af[4 * h + 2],
-                                   af[4 * h + 3], ptx::e4m3x2_to_f16x2(bv, 0),
-                                   ptx::e4m3x2_to_f16x2(bv, 1));
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t bv = b[ks][2 * j + h];
+                ptx::mma_f16_16x8x16(tmp, af[4 * h], af[4 * h + 1], af[4 * h + 2],
+                                     af[4 * h + 3], ptx::e4m3x2_to_f16x2(bv, 0),
+                                     ptx::e4m3x2_to_f16x2(bv, 1));
+              }
+              const float sb0 = e8m0_to_float((sx[j][0] >> sh) & 0xFFu);
+              const float sb1 = e8m0_to_float((sx[j][1] >> sh) & 0xFFu);
+              acc[ks][j][0] = fmaf(tmp[0] * sa0, sb0, acc[ks][j][0]);
+              acc[ks][j][1] = fmaf(tmp[1] * sa0, sb1, acc[ks][j][1]);
+              acc[ks][j][2] = fmaf(tmp[2] * sa1, sb0, acc[ks][j][2]);
+              acc[ks][j][3] = fmaf(tmp[3] * sa1, sb1, acc[ks][j][3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t bv = b[ks][2 * j + h];
+                ptx::mma_f16_16x8x16(acc[ks][j], af[4 * h], af[4 * h + 1], af[4 * h + 2],
+                                     af[4 * h + 3], ptx::e4m3x2_to_f16x2(bv, 0),
+                                     ptx::e4m3x2_to_f16x2(bv, 1));
+              }
             }
           }
         }
@@ -857,28 +935,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   }
 }
 
-template <int MPAD>
+// MXFP8 (F = kFmtMX) is launched only for K % 128 == 0 (chunk views).
+template <int MPAD, int F>
 int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
+  constexpr bool MX = F == small::kFmtMX;
+  const char *name = MX ? "mxfp8_gemm: " : "fp8_gemm: ";
   std::string err;
-  CUtensorMap tw, tx;
+  CUtensorMap tw, tx, twsf, txsf;
   // chunk views (one copy per stage and operand) when K allows; 2-D boxes otherwise
   bool wide = a.K % CHUNK == 0 && make_tmap_chunks_u8(&tw, a.wq, a.K, a.N, WR, SC, &err) &&
               make_tmap_chunks_u8(&tx, a.xq, a.K, a.M, MPAD, SC, &err);
+  if (MX && !wide) {
+    set_error(std::string(name) + "warp-level kernel needs K % 128 == 0" +
+              (err.empty() ? "" : ": " + err));
+    return 4;
+  }
   if (!wide && (!make_tmap_2d_u8(&tw, a.wq, a.K, a.N, CHUNK, WR, &err) ||
                 !make_tmap_2d_u8(&tx, a.xq, a.K, a.M, CHUNK, MPAD, &err))) {
-    set_error("fp8_gemm: " + err);
+    set_error(name + err);
     return 4;
+  }
+  if constexpr (MX) {
+    const uint64_t ncb = static_cast<uint64_t>((a.K / 32 + 3) / 4);
+    if (!make_tmap_sf_box(&twsf, a.wsf, a.N, ncb, 64, SC, &err) ||
+        !make_tmap_sf_box(&txsf, a.xsf, a.M, ncb, 64, SC, &err)) {
+      set_error(name + err);
+      return 4;
+    }
+  } else {  // unused by the kernel: any valid map
+    twsf = tw;
+    txsf = tw;
   }
   static std::once_flag once[64];
   static cudaError_t setup_err[64];
   const int d = dev.device & 63;
   std::call_once(once[d], [&] {
-    setup_err[d] = cudaFuncSetAttribute(fp8_gemm_rows_kernel<MPAD>,
+    setup_err[d] = cudaFuncSetAttribute(fp8_gemm_rows_kernel<MPAD, F>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem_bytes(MPAD)));
+                                        static_cast<int>(smem_bytes(MPAD, MX)));
   });
   if (setup_err[d] != cudaSuccess) {
-    set_error(std::string("fp8_gemm: rows kernel setup: ") + cudaGetErrorString(setup_err[d]));
+    set_error(std::string(name) + "rows kernel setup: " + cudaGetErrorString(setup_err[d]));
     return 4;
   }
   Params p;
@@ -901,7 +998,7 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((a.N + WR - 1) / WR));
   cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = smem_bytes(MPAD);
+  cfg.dynamicSmemBytes = smem_bytes(MPAD, MX);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   int n = 0;
@@ -912,9 +1009,10 @@ int launch(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool p
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  const cudaError_t ce = cudaLaunchKernelEx(&cfg, fp8_gemm_rows_kernel<MPAD>, tw, tx, p);
+  const cudaError_t ce =
+      cudaLaunchKernelEx(&cfg, fp8_gemm_rows_kernel<MPAD, F>, tw, tx, twsf, txsf, p);
   if (ce != cudaSuccess) {
-    set_error(std::string("fp8_gemm: rows kernel launch failed: ") + cudaGetErrorString(ce));
+    set_error(std::string(name) + "rows kernel launch failed: " + cudaGetErrorString(ce));
     return 4;
   }
   return 0;
@@ -926,9 +1024,16 @@ int launch_gemm_small(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   DeviceInfo dev;
   if (!current_device_info(&dev)) return 5;
   if (a.nv) return small::launch<small::kFmtNV>(a, dev, stream, pdl);
-  if (a.mx) return small::launch<small::kFmtMX>(a, dev, stream, pdl);
-  if (a.M <= 8) return rows::launch<8>(a, dev, stream, pdl);
-  if (a.M <= rows::MAX_TOK) return rows::launch<16>(a, dev, stream, pdl);
+  if (a.mx) {
+    // MXFP8 on the warp-level kernel up to 8 tokens (one 8-token fragment set); at 9-16
+    // tokens it measured faster alone but slower behind the quantizer than the
+    // split-K kernel
+    if (a.M <= 8 && a.K % rows::CHUNK == 0)
+      return rows::launch<8, small::kFmtMX>(a, dev, stream, pdl);
+    return small::launch<small::kFmtMX>(a, dev, stream, pdl);
+  }
+  if (a.M <= 8) return rows::launch<8, small::kFmtE4M3>(a, dev, stream, pdl);
+  if (a.M <= rows::MAX_TOK) return rows::launch<16, small::kFmtE4M3>(a, dev, stream, pdl);
   return small::launch<small::kFmtE4M3>(a, dev, stream, pdl);
 }
 

@@ -1,10 +1,11 @@
-"""The GEMM for at most 16 tokens (warp-level e4m3 MMAs over 16 whole weight rows per CTA,
-K streamed in 512-byte stages, the four warps' partials summed in shared memory), on the
-GPU against the CPU oracle (csrc/fp8_gemm.cu:65-80 restated, exact sums), with
-max|got - ref| / max|ref| <= 1e-2:
-ragged N (not a multiple of the 16-row CTA tile), K not a multiple of the 128-byte box
-or of the 512-byte stage, both token fragment widths (8 and 16), every bias and output
-type, column blocks of a wider output, repeatability, and the fused entry point."""
+"""The GEMM for at most 16 tokens (warp-level f16 MMAs on exactly converted e4m3 codes
+over 16 whole weight rows per CTA, K streamed in 1024-byte stages, the eight warps'
+partials summed in shared memory), on the GPU against the CPU oracle (csrc/fp8_gemm.cu:
+65-80 restated, exact sums), with max|got - ref| / max|ref| <= 1e-2: ragged N (not a
+multiple of the 16-row CTA tile), K not a multiple of the 128-byte box or of the stage
+(2-D boxes instead of the chunk view), both token fragment widths (8 and 16), every bias
+and output type, column blocks of a wider output, repeatability, the fused entry point;
+and its MXFP8 form (at most 8 tokens) bit-exact with power-of-two block scales."""
 from __future__ import annotations
 
 import pytest
@@ -120,3 +121,58 @@ def test_rows_zero_and_extreme_tokens(oracle):
     for m in range(11):
         if m != 2:
             assert max_rel(out[m].float().cpu(), ref[m]) <= OUT_TOL, m
+
+
+def _pow2_mx_blocks(rows, K, g):
+    """Integers {0, 1, 2, 3} x sign x 2^e per 32-element block (e in {0, 1}), each block
+    led by +-6 x 2^e: exact in e4m3 after the MX scale 2^(e - 6), and every sum of
+    products exact in fp32, so the output is the float64 product rounded once."""
+    lv = torch.tensor([0.0, 1.0, 2.0, 3.0], device="cuda")
+    v = lv[torch.randint(0, 4, (rows, K), device="cuda", generator=g)]
+    v[:, ::32] = 6.0
+    v = v * (torch.randint(0, 2, (rows, K), device="cuda", generator=g) * 2 - 1)
+    e = torch.randint(0, 2, (rows, K // 32), device="cuda", generator=g).float()
+    return (v * torch.exp2(e).repeat_interleave(32, dim=1)).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M", [1, 5, 8, 9, 16])
+@pytest.mark.parametrize("N,K", [(520, 3072), (136, 1024), (3072, 2048)])
+def test_rows_mxfp8_exact_power_of_two_scales(M, N, K):
+    """MXFP8 with few tokens (M <= 8 on the warp-level kernel, 9 and 16 on the split-K
+    kernel): each 32-byte K-step of the warp-level kernel is one block whose sum takes the
+    weight row's and the token's scale. Scales 1 or 2 per row and block, several stages,
+    weight rows in both halves and all four 32-row groups of their scale tiles, ragged N:
+    a scale taken from the wrong row, token or block changes the bits."""
+    import fp8linear_b200 as f
+
+    g = torch.Generator(device="cuda").manual_seed(1000 + 7 * M + N)
+    x = _pow2_mx_blocks(M, K, g)
+    w = _pow2_mx_blocks(N, K, g)
+    xq, xs = f.quantize_mxfp8(x)
+    wq, ws = f.quantize_weight_mxfp8(w)
+    out = f.mxfp8_gemm(xq, xs, wq, ws, None)
+    torch.cuda.synchronize()
+    ref = (x.double().cpu() @ w.double().cpu().T).float().to(torch.bfloat16)
+    assert torch.equal(out.cpu(), ref)
+    assert torch.equal(f.mxfp8_linear(x, wq, ws, None), out)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 3072), (7, 1000, 4096), (8, 44, 8192)])
+def test_rows_mxfp8_vs_oracle(oracle, M, N, K):
+    """MXFP8 on the warp-level kernel on normal data against the oracle's MX product
+    (csrc/fp8_gemm.cu:233-333 restated), with bias; two calls give the same bits."""
+    import fp8linear_b200 as f
+
+    gen = torch.Generator(device="cuda").manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    xq, xs = f.quantize_mxfp8(x)
+    wq, ws = f.quantize_weight_mxfp8(w)
+    out = f.mxfp8_gemm(xq, xs, wq, ws, b)
+    again = f.mxfp8_gemm(xq, xs, wq, ws, b)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
+    ref = oracle.np_mxfp8_gemm(codes(xq), xs.cpu().numpy(), codes(wq), ws.cpu().numpy())
+    ref = ref + f32(b)[None, :]
+    assert max_rel(out.cpu(), torch.from_numpy(ref)) <= OUT_TOL
