@@ -565,6 +565,8 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
   if (e == cudaSuccess) e = cudaStreamWaitEvent(h->comp, h->start, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(h->down, h->start, 0);
   const int64_t chunks = (M + rows - 1) / rows;
+  DeviceInfo dev;
+  const int host_tile_n = current_device_info(&dev) ? pair_tile_n(M, N, dev.sm_count) : 256;
   rc = FP8LIN_OK;
   for (int64_t i = 0; i < chunks && e == cudaSuccess; ++i) {
     const int s = static_cast<int>(i & 1);
@@ -589,6 +591,7 @@ int fp8lin_fp8_linear_host(const void *x_host, int x_dtype, const void *wq, cons
     // A ragged last chunk of a multi-chunk call takes the CTA-pair kernel like the full
     // chunks, so every row is summed in the order the whole-M call uses.
     a.pairs_only = chunks > 1;
+    if (chunks > 1) a.tile_n = host_tile_n;  // the whole call's tile width, every chunk
     a.weights_before_wait = true;  // the previous kernel is this chunk's quantizer
     rc = launch_gemm(a, h->comp, true);
     if (rc != FP8LIN_OK) break;  // launch_gemm set the message

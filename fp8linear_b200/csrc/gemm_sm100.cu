@@ -52,7 +52,7 @@ __device__ unsigned int g_gemm_status;  // watchdog bits (1 producer, 2 mma, 4 e
 namespace gemm {
 
 constexpr int BM = 128;  // rows of A per CTA
-constexpr int BN = 256;  // output columns per tile
+constexpr int BN = 256;  // output columns per tile (the widest; per-token e4m3 also 192)
 constexpr int BK = 128;  // bytes == e4m3 elements per K-block (one 128B swizzle row)
 constexpr int UMMA_K = 32;
 constexpr int EPI_WARPS = 4;
@@ -80,12 +80,13 @@ constexpr uint32_t RING_BYTES = 160 * 1024;      // operand ring (both shapes)
 // the epilogue reads the shared chunk first and releases it before the rest (bar_tovl).
 enum : int { kFmtE4M3 = 0, kFmtMX = 1, kFmtNV = 2 };
 
-template <int CG, int F = kFmtE4M3>
+template <int CG, int F = kFmtE4M3, int NB = BN>
 struct Cfg {
   static constexpr bool MX = F != kFmtE4M3;                    // block-scaled (MX or NV)
   static constexpr bool NV = F == kFmtNV;
+  static constexpr int TILE_N = NB;                            // output columns per tile
   static constexpr int SF_TILES = NV ? 4 : 1;                  // scale tiles per K-block, row block
-  static constexpr int B_ROWS = BN / CG;                       // B rows this CTA loads
+  static constexpr int B_ROWS = NB / CG;                       // B rows this CTA loads
   static constexpr uint32_t B_STAGE = B_ROWS * BK;             // 32 KB (CG 1) / 16 KB (CG 2)
   static constexpr uint32_t SFA_STAGE = MX ? 512u * SF_TILES : 0u;   // A scales of the K-block
   static constexpr uint32_t SFB_STAGE = MX ? 1024u * SF_TILES : 0u;  // B scales, all 256 rows
@@ -106,16 +107,17 @@ struct Cfg {
   static constexpr uint32_t OFF_TMEM_SLOT = OFF_BAR + NUM_BARS * 8;
   static constexpr uint32_t OFF_ABORT = OFF_TMEM_SLOT + 4;
   static constexpr uint32_t SMEM_BYTES = OFF_ABORT + 4 + 1024;  // + base alignment slack
-  static constexpr uint32_t IDESC = ptx::idesc_e4m3_f32(TILE_M, BN);
+  static constexpr uint32_t IDESC = ptx::idesc_e4m3_f32(TILE_M, NB);
   static constexpr uint32_t IDESC_MX =
       NV ? ptx::idesc_nv_e2m1(TILE_M, BN) : ptx::idesc_mx_e4m3(TILE_M, BN, 0);
-  static constexpr uint32_t ACC1_COL = MX ? BN - EPI_COLS : BN;  // accumulator 1's column
+  static constexpr uint32_t ACC1_COL = MX ? BN - EPI_COLS : NB;  // accumulator 1's column
   static constexpr uint32_t SFA_COL = 2 * BN - EPI_COLS;          // block scale factors:
   static constexpr uint32_t SFB_COL = SFA_COL + 4 * SF_TILES;     // A 4/tile, B 8/tile
   static_assert(STAGES * STAGE <= RING, "ring");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(OFF_B % 1024 == 0 && OFF_EPI % 1024 == 0, "swizzle atoms need 1024 B alignment");
   static_assert(!MX || SFB_COL + 8 * SF_TILES <= TMEM_COLS, "TMEM budget");
+  static_assert(NB % EPI_COLS == 0 && NB <= BN && (NB == BN || !MX), "tile width");
 };
 
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
@@ -167,7 +169,7 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
   }
 }
 
-template <int CG, int F>
+template <int CG, int F, int NB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const __grid_constant__ CUtensorMap tmap_sfa,
                     const __grid_constant__ CUtensorMap tmap_sfb,
                     const __grid_constant__ CUtensorMap tmap_out2, const Params p) {
-  using C = Cfg<CG, F>;
+  using C = Cfg<CG, F, NB>;
   constexpr bool MX = C::MX;
   constexpr bool NV = C::NV;
   extern __shared__ uint8_t smem_raw[];
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int mt, nt;
         tile_coords(p, t, mt, nt);
         const int a_row = mt * C::TILE_M + static_cast<int>(rank) * BM;
-        const int b_row = nt * BN + static_cast<int>(rank) * C::B_ROWS;
+        const int b_row = nt * NB + static_cast<int>(rank) * C::B_ROWS;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!ptx::mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1u, abort, kWaitLimitNs)) {
             if (!*abort) record_timeout(1u, abort);
@@ -424,8 +426,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Stage this tile's per-column w_scale and bias (as fp32) in the warp's own
       // smem slice while the main loop runs; columns past N read as 0.
       __syncwarp();
-      for (int i = lane; i < BN; i += 32) {
-        const int n = nt * BN + i;
+      for (int i = lane; i < NB; i += 32) {
+        const int n = nt * NB + i;
         const bool in = n < p.N;
         par_ws[i] = in ? (MX ? 1.0f : __ldg(p.ws + n)) : 0.0f;  // MX: scales are in acc
         par_b[i] = in ? load_bias(p.bias, p.bias_dtype, n) : 0.0f;
@@ -458,12 +460,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ovl_done = true;
       };
 #pragma unroll 1
-      for (int ci = 0; ci < BN / EPI_COLS; ++ci) {
+      for (int ci = 0; ci < NB / EPI_COLS; ++ci) {
         if (MX && ci == 1 && !ovl_done) release_overlap();
         // MX, accumulator 0: chunks in descending order, the shared (last) one first; the
         // pairs stored together, {3, 2} and {1, 0}, stay adjacent
-        const int c = (MX && acc == 0) ? BN / EPI_COLS - 1 - ci : ci;
-        const int n0 = nt * BN + c * EPI_COLS;
+        const int c = (MX && acc == 0) ? NB / EPI_COLS - 1 - ci : ci;
+        const int n0 = nt * NB + c * EPI_COLS;
         if (!rows_live) break;   // warp-uniform
         if (n0 >= p.N) {
           if (MX) continue;      // chunk order is not ascending
@@ -711,7 +713,7 @@ struct LaunchInfo {
   int max_groups = 0;
 };
 
-template <int CG, int F>
+template <int CG, int F, int NB>
 LaunchInfo &launch_info(int device, int sm_count) {
   static LaunchInfo info[64];
   static std::mutex mu;
@@ -719,14 +721,15 @@ LaunchInfo &launch_info(int device, int sm_count) {
   LaunchInfo &li = info[device & 63];
   if (!li.ready) {
     li.ready = true;
-    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(Cfg<CG, F>::SMEM_BYTES));
+    li.err = cudaFuncSetAttribute(fp8_gemm_kernel<CG, F, NB>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(Cfg<CG, F, NB>::SMEM_BYTES));
     li.max_groups = sm_count / CG;
     if (li.err == cudaSuccess && CG == 2) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(sm_count);
       cfg.blockDim = dim3(NUM_THREADS);
-      cfg.dynamicSmemBytes = Cfg<CG, F>::SMEM_BYTES;
+      cfg.dynamicSmemBytes = Cfg<CG, F, NB>::SMEM_BYTES;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = CG;
@@ -735,7 +738,7 @@ LaunchInfo &launch_info(int device, int sm_count) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG, F>, &cfg);
+      li.err = cudaOccupancyMaxActiveClusters(&clusters, fp8_gemm_kernel<CG, F, NB>, &cfg);
       if (li.err == cudaSuccess) li.max_groups = std::min(li.max_groups, clusters);
       if (li.err == cudaSuccess && li.max_groups < 1) li.err = cudaErrorInvalidConfiguration;
     }
@@ -743,9 +746,9 @@ LaunchInfo &launch_info(int device, int sm_count) {
   return li;
 }
 
-template <int CG, int F>
+template <int CG, int F, int NB = BN>
 int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, bool pdl) {
-  using C = Cfg<CG, F>;
+  using C = Cfg<CG, F, NB>;
   constexpr bool MX = C::MX;
   const char *name = C::NV ? "nvfp4_gemm: " : MX ? "mxfp8_gemm: " : "fp8_gemm: ";
   std::string err;
@@ -797,14 +800,15 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
   p.N = static_cast<int>(a.N);
   p.K = static_cast<int>(a.K);
   p.m_tiles = static_cast<int>((a.M + C::TILE_M - 1) / C::TILE_M);
-  p.n_tiles = static_cast<int>((a.N + BN - 1) / BN);
+  p.n_tiles = static_cast<int>((a.N + NB - 1) / NB);
   p.k_blocks = static_cast<int>((kbytes + BK - 1) / BK);
   p.ncb = static_cast<int>(ncb);
   p.n_fastest = a.M >= a.N ? 1 : 0;
   p.direct_store = direct ? 1 : 0;
   CUtensorMap tout2 = tout;
   p.wide_store = 0;
-  if (!direct && a.n_peers == 0 && a.N % 128 == 0) {
+  // (paired 64-column chunks stay inside a tile only at width 256)
+  if (NB == BN && !direct && a.n_peers == 0 && a.N % 128 == 0) {
     std::string werr;  // a view the driver does not take: 64-column boxes instead
     if (make_tmap_out_wide(&tout2,
                            a.out_dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -829,7 +833,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
     set_error("fp8_gemm: too many output tiles");
     return 2;
   }
-  LaunchInfo &li = launch_info<CG, F>(dev.device, dev.sm_count);
+  LaunchInfo &li = launch_info<CG, F, NB>(dev.device, dev.sm_count);
   if (li.err != cudaSuccess) {
     set_error(std::string("fp8_gemm: kernel setup: ") + cudaGetErrorString(li.err));
     return 4;
@@ -862,7 +866,7 @@ int launch_shape(const GemmArgs &a, const DeviceInfo &dev, cudaStream_t stream, 
     tsfb = ta;
   }
   cudaError_t ce =
-      cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, F>, ta, tb, tout, tsfa, tsfb, tout2, p);
+      cudaLaunchKernelEx(&cfg, fp8_gemm_kernel<CG, F, NB>, ta, tb, tout, tsfa, tsfb, tout2, p);
   if (ce != cudaSuccess) {
     set_error(std::string("fp8_gemm: launch failed: ") + cudaGetErrorString(ce));
     return 4;
@@ -953,7 +957,20 @@ int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl) {
   }
   if (a.M <= gemm::BM && !a.pairs_only)
     return gemm::launch_shape<1, gemm::kFmtE4M3>(a, dev, stream, pdl);
+  const int tn = a.n_peers > 0 ? 256 : a.tile_n > 0 ? a.tile_n : pair_tile_n(a.M, a.N, dev.sm_count);
+  if (tn == 192) return gemm::launch_shape<2, gemm::kFmtE4M3, 192>(a, dev, stream, pdl);
   return gemm::launch_shape<2, gemm::kFmtE4M3>(a, dev, stream, pdl);
+}
+
+int pair_tile_n(int64_t M, int64_t N, int sm_count) {
+  // 192-column tiles when all of them fit in one wave of CTA pairs: more pairs busy, each
+  // with a shorter tile (sweep_M1024 13.95 against 14.52 us). Past one wave the kernel is
+  // bound by the total operand stream from L2, which narrower tiles enlarge (a 2304 x
+  // 15360 -> 3072 linear: 88.3 against 87.5 us, though 256-column tiles leave its second
+  // wave half empty).
+  const int64_t pairs = std::max(1, sm_count / 2);
+  const int64_t mt = (M + 2 * gemm::BM - 1) / (2 * gemm::BM);
+  return mt * ((N + 191) / 192) <= pairs ? 192 : 256;
 }
 
 namespace {

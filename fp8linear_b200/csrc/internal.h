@@ -105,6 +105,9 @@ struct GemmArgs {
   // quantizer of the same call: it lets its dependents launch only after its own wait
   // has returned, so every kernel before it (a weight writer included) has completed.
   bool weights_before_wait = false;
+  // Per-token e4m3 CTA-pair tiles: output columns per tile (256 or 192; 0: pair_tile_n of
+  // this call's M and N). A call split into row chunks passes the whole call's choice.
+  int tile_n = 0;
 };
 constexpr int kMaxPeers = 7;
 // Token counts up to which the GEMM may run a few-token kernel (it streams the weights once).
@@ -115,6 +118,8 @@ constexpr int64_t kFewTokenMaxM = 256;
 // before writing anything. Returns an fp8lin_status code and sets the error message on
 // failure.
 int launch_gemm(const GemmArgs &a, cudaStream_t stream, bool pdl);
+// Tile width (256 or 192 columns) of the per-token e4m3 CTA-pair kernel for an [M, N] output.
+int pair_tile_n(int64_t M, int64_t N, int sm_count);
 // Reads (and optionally clears) the GEMM watchdog bits of the current device.
 cudaError_t read_gemm_status(unsigned int *bits, bool clear);
 

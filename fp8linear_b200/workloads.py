@@ -12,6 +12,8 @@ are the FLUX linears the reference's own hardware scripts time
   flux_linear1   M=18432, K=3072  -> N=21504   x ~ N(0,1), 0.5% channels x50
   flux_linear2   M=18432, K=15360 -> N=3072    x ~ N(0,1), 0.5% channels x50
   sweep_M<m>     M=m,     K=3072  -> N=3072    x ~ N(0,1), m in SWEEP_M
+  flux_linear2_rank8  M=2304, K=15360 -> N=3072  linear2 rows of one of 8 GPUs splitting
+                 the 18432 (batch-4 single-stream block) rows, as flux_linear2
 
 Weights are N(0, 0.02) in bf16, bias N(0, 0.02) in bf16. Each workload uses its own
 generator seeded with ``seed``; values are drawn on ``gen_device`` so the same
@@ -62,6 +64,7 @@ def _build() -> dict[str, Workload]:
         Workload("flux_linear2", 18432, 15360, 3072, "normal", 0.005, 50.0),
     ]
     w += [Workload(f"sweep_M{m}", m, 3072, 3072) for m in SWEEP_M]
+    w.append(Workload("flux_linear2_rank8", 18432 // 8, 15360, 3072, "normal", 0.005, 50.0))
     return {x.name: x for x in w}
 
 

@@ -70,12 +70,15 @@ def test_gemm_shapes_vs_oracle(M, N, K, oracle):
     assert err <= OUT_TOL, err
 
 
-@pytest.mark.parametrize("M,N", [(333, 384), (200, 1152)])
+@pytest.mark.parametrize("M,N", [(333, 384), (200, 1152), (4608, 3456), (1000, 1280)])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
 def test_gemm_paired_stores_edges(M, N, out_dtype, capi, oracle):
-    """Output widths that are multiples of 128 but not of the 256-column tile (the last
-    tile's second chunk pair lies past N and is not stored), rows not a multiple of 32,
-    both output types: the paired 3-D stores write exactly the [M, N] block."""
+    """Output widths that are multiples of 128 but not of the 256-column tile, rows not a
+    multiple of 32, both output types. 4608 x 3456 keeps 256-column pair tiles (more than
+    one wave), whose last tile's second chunk pair lies past N and is not stored: the
+    paired 3-D stores write exactly the [M, N] block. The others fit one wave of
+    192-column tiles, stored chunk by chunk; 1000 x 1280 has a partial last tile (128 of
+    its 192 columns)."""
     xq, xs, wq, ws, b = _operands(M, N, 512, seed=M + N)
     out = capi.fp8_gemm(xq, xs, wq, ws, b, out_dtype=out_dtype)
     torch.cuda.synchronize()
@@ -96,7 +99,8 @@ def test_gemm_bias_and_out_dtypes(bias_dtype, out_dtype, capi):
 
 @pytest.mark.parametrize("name", ["flux_qkv", "flux_fc1", "flux_fc2", "flux_linear1",
                                   "flux_linear2", "sweep_M1", "sweep_M16", "sweep_M128",
-                                  "sweep_M1024", "sweep_M4096", "sweep_M16384", "sweep_M65536"])
+                                  "sweep_M1024", "sweep_M4096", "sweep_M16384", "sweep_M65536",
+                                  "flux_linear2_rank8"])
 def test_gemm_workloads_vs_torch_fp32(name):
     from fp8linear_b200 import ops
 
