@@ -931,7 +931,9 @@ template <typename T>
 __global__ void __launch_bounds__(32 * kMxWarps) quant_mx_kernel(
     const T *__restrict__ x, uint8_t *__restrict__ xq, uint8_t *__restrict__ sf, int64_t M,
     int K, int64_t rows_pad, int segs, int ncb, int trigger) {
-  if (trigger) ptx::grid_launch_dependents();
+  // trigger bits as the per-token kernels': 1 = release the dependents, 2 = wait first
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t wid = static_cast<int64_t>(blockIdx.x) * kMxWarps + (threadIdx.x >> 5);
   const int64_t row = wid / segs;
@@ -1042,7 +1044,9 @@ template <typename T>
 __global__ void __launch_bounds__(32 * kMxWarps) quant_nv_kernel(
     const T *__restrict__ x, uint8_t *__restrict__ xq, uint8_t *__restrict__ sf, int64_t M,
     int K, int64_t rows_pad, int segs, int ncb, int trigger) {
-  if (trigger) ptx::grid_launch_dependents();
+  // trigger bits as the per-token kernels': 1 = release the dependents, 2 = wait first
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t wid = static_cast<int64_t>(blockIdx.x) * kMxWarps + (threadIdx.x >> 5);
   const int64_t row = wid / segs;
@@ -1105,10 +1109,10 @@ cudaError_t launch_nv_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, ui
   const int64_t warps = rows_pad * segs;
   const int64_t blocks = (warps + kMxWarps - 1) / kMxWarps;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  quant_nv_kernel<T><<<static_cast<unsigned>(blocks), 32 * kMxWarps, 0, stream>>>(
-      reinterpret_cast<const T *>(x), xq, sf, M, static_cast<int>(K), rows_pad, segs, ncb,
-      trigger ? 1 : 0);
-  return cudaGetLastError();
+  // a programmatic dependent of the kernel before it, as the per-token quantizer
+  return launch_dependent(quant_nv_kernel<T>, static_cast<unsigned>(blocks), 32 * kMxWarps, 0, stream,
+                          reinterpret_cast<const T *>(x), xq, sf, M, static_cast<int>(K),
+                          rows_pad, segs, ncb, (trigger ? 1 : 0) | 2);
 }
 
 template <typename T>
@@ -1120,10 +1124,10 @@ cudaError_t launch_mx_typed(const void *x, int64_t M, int64_t K, uint8_t *xq, ui
   const int64_t warps = rows_pad * segs;
   const int64_t blocks = (warps + kMxWarps - 1) / kMxWarps;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  quant_mx_kernel<T><<<static_cast<unsigned>(blocks), 32 * kMxWarps, 0, stream>>>(
-      reinterpret_cast<const T *>(x), xq, sf, M, static_cast<int>(K), rows_pad, segs, ncb,
-      trigger ? 1 : 0);
-  return cudaGetLastError();
+  // a programmatic dependent of the kernel before it, as the per-token quantizer
+  return launch_dependent(quant_mx_kernel<T>, static_cast<unsigned>(blocks), 32 * kMxWarps, 0, stream,
+                          reinterpret_cast<const T *>(x), xq, sf, M, static_cast<int>(K),
+                          rows_pad, segs, ncb, (trigger ? 1 : 0) | 2);
 }
 
 // ---------------------------------------------------------------- LayerNorm + modulation
@@ -1217,7 +1221,9 @@ __global__ void __launch_bounds__(kLnThreads) ln_mod_quant_kernel(
     const T *__restrict__ x, const T *__restrict__ shift, const T *__restrict__ scale, int64_t M,
     int K, int64_t rows_per_batch, float eps, uint8_t *__restrict__ xq, float *__restrict__ xs,
     int trigger) {
-  if (trigger) ptx::grid_launch_dependents();
+  // trigger bits as the per-token kernels': 1 = release the dependents, 2 = wait first
+  if (trigger & 2) ptx::grid_dependency_wait();
+  if (trigger & 1) ptx::grid_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (kLnThreads / 32) + (threadIdx.x >> 5);
   if (row >= M) return;  // warp-uniform
@@ -1323,10 +1329,11 @@ cudaError_t launch_ln_cpl(const void *x, const void *shift, const void *scale, i
                           cudaStream_t stream, bool trigger) {
   const int64_t blocks = (M + kLnThreads / 32 - 1) / (kLnThreads / 32);
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  ln_mod_quant_kernel<T, CPL><<<static_cast<unsigned>(blocks), kLnThreads, 0, stream>>>(
-      reinterpret_cast<const T *>(x), reinterpret_cast<const T *>(shift),
-      reinterpret_cast<const T *>(scale), M, K, rows_per_batch, eps, xq, xs, trigger ? 1 : 0);
-  return cudaGetLastError();
+  // a programmatic dependent of the kernel before it, as the per-token quantizer
+  return launch_dependent(ln_mod_quant_kernel<T, CPL>, static_cast<unsigned>(blocks), kLnThreads,
+                          0, stream, reinterpret_cast<const T *>(x),
+                          reinterpret_cast<const T *>(shift), reinterpret_cast<const T *>(scale),
+                          M, K, rows_per_batch, eps, xq, xs, (trigger ? 1 : 0) | 2);
 }
 
 template <typename T>
