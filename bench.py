@@ -50,6 +50,8 @@ FLUSH_BYTES = 256 << 20
 # idle time before each timed leg of a sweep: a bandwidth-bound kernel timed right after
 # tens of milliseconds of full-power GEMM replays reads up to 30 % slow
 SWEEP_PAUSE_S = 0.5
+# idle time before each config-4 leg (clocks recover after long full-power GEMM graphs)
+CFG_PAUSE_S = 1.0
 NOMINAL_FP8_TFLOPS = 4500.0
 FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 L2_FALLBACK = 126 << 20
@@ -564,8 +566,13 @@ def mshard_cfg4(args, world, rank, dev, barrier) -> dict:
     21504, linear2 18432 x 15360 -> 3072) with the GLOBAL 18432 token rows split over the
     ranks (strong scaling), weights replicated, no collective. Each rank times its row
     block (steps back to back over rotating operand sets, as the headline); the job time
-    is the max over ranks. Rank 0 also times all 18432 rows alone on its GPU, the
-    one-GPU figure the efficiency is taken against (t1 / (N x tN))."""
+    is the max over ranks. Rank 0 then times all 18432 rows alone on its GPU, the one-GPU
+    figure the efficiency is taken against (t1 / (N x tN)). Every timed leg starts after
+    CFG_PAUSE_S idle on every rank: right after seconds of full-power GEMM graphs a GPU
+    runs the next graph at lower clocks (one B200: the 2304-row linear2 block 102 us per
+    step after a pause, 132 right after one 18432-row linear1 graph, 153 at 1500 MHz
+    after four), and rank 0 would otherwise time its block right after its linear1
+    reference."""
     import dataclasses
 
     import fp8linear_b200 as f
@@ -573,51 +580,67 @@ def mshard_cfg4(args, world, rank, dev, barrier) -> dict:
 
     W = _workloads()
     stream = torch.cuda.current_stream(dev)
-    out = {}
-    for name in ("flux_linear1", "flux_linear2"):
+
+    def pause():
+        barrier()
+        time.sleep(CFG_PAUSE_S)
+        barrier()
+
+    def step(st):
+        return f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"])
+
+    names = ("flux_linear1", "flux_linear2")
+    t_n = {}
+    for name in names:  # every rank's own row block, all ranks at once
         wl = W.WORKLOADS[name]
         s0, e0 = row_range(wl.M, world, rank)
         wl_r = dataclasses.replace(wl, M=e0 - s0)
-
-        def step(st):
-            return f.fp8_linear(st["x"], st["wq"], st["ws"], st["b"])
-
         sets = operand_sets(wl_r, set_count(per_set_bytes(wl_r), dev), x_seed0=1000 * rank,
                             quantize_x=False)
         for i in range(args.warmup):
             step(sets[i % len(sets)])
-        barrier()
-        t_n = _max_over_ranks([_graph_ms(step, sets, args.steps, stream, barrier)], world,
-                              dev)[0] / args.steps
+        pause()
+        t_n[name] = _max_over_ranks([_graph_ms(step, sets, args.steps, stream, barrier)],
+                                    world, dev)[0] / args.steps
         del sets
         torch.cuda.empty_cache()
-        t_1 = t_n
-        if world > 1:
+    t_1 = dict(t_n)
+    if world > 1:  # the one-GPU references: all rows on rank 0's GPU
+        import torch.distributed as dist
+
+        for name in names:
+            wl = W.WORKLOADS[name]
             t1 = torch.zeros(1, device=dev, dtype=torch.float64)
+            sets = None
             if rank == 0:
                 sets = operand_sets(wl, set_count(per_set_bytes(wl), dev), quantize_x=False)
                 for i in range(args.warmup):
                     step(sets[i % len(sets)])
                 torch.cuda.synchronize(dev)
+            pause()
+            if rank == 0:
                 t1[0] = _graph_ms(step, sets, args.steps, stream,
                                   lambda: torch.cuda.synchronize(dev)) / args.steps
-                del sets
-                torch.cuda.empty_cache()
-            import torch.distributed as dist
-
+            del sets
+            torch.cuda.empty_cache()
             dist.broadcast(t1, 0)
-            t_1 = float(t1.item())
-        tf_n = wl.flops / (t_n * 1e-3) / 1e12
-        tf_1 = wl.flops / (t_1 * 1e-3) / 1e12
+            t_1[name] = float(t1.item())
+    out = {}
+    for name in names:
+        wl = W.WORKLOADS[name]
+        tf_n = wl.flops / (t_n[name] * 1e-3) / 1e12
+        tf_1 = wl.flops / (t_1[name] * 1e-3) / 1e12
         out[name.replace("flux_", "")] = {
             "global_M": wl.M, "K": wl.K, "N": wl.N, "rows_per_gpu_max": -(-wl.M // world),
-            "value": round(tf_n, 1), "unit": "TFLOP/s", "ms_per_step": round(t_n, 4),
-            "one_gpu_tflops": round(tf_1, 1), "one_gpu_ms": round(t_1, 4),
-            "speedup": round(t_1 / t_n, 3), "efficiency": round(t_1 / (world * t_n), 4)}
+            "value": round(tf_n, 1), "unit": "TFLOP/s", "ms_per_step": round(t_n[name], 4),
+            "one_gpu_tflops": round(tf_1, 1), "one_gpu_ms": round(t_1[name], 4),
+            "speedup": round(t_1[name] / t_n[name], 3),
+            "efficiency": round(t_1[name] / (world * t_n[name]), 4)}
     out["scaling"] = "strong"
     out["how"] = ("fp8_linear (quantizer + GEMM) on each rank's block of the global 18432 "
                   f"rows, {args.steps} steps back to back in one CUDA graph over rotating "
-                  "operand sets, max over ranks; one_gpu: all rows on rank 0's GPU alone")
+                  f"operand sets, max over ranks; one_gpu: all rows on rank 0's GPU alone, "
+                  f"timed after both row-block legs; {CFG_PAUSE_S} s idle before every leg")
     return out
 
 
