@@ -12,6 +12,11 @@ calls bit-identical, and the fused linear bit-identical to quantizer + GEMM.
 Token counts are drawn per bucket of the dispatcher: 1-16 (warp-level kernel), 17-128
 (split-K few-token kernel), 129-256 (few-token kernel with two token blocks, or CTA
 pairs when it gets no K-split), 257-3000 (CTA pairs, 192- or 256-column tiles).
+
+The other entry points get random shapes too: the host-buffer linear and the
+no-allocation linear must give the device linear's bits, and the fused LayerNorm +
+modulation quantizer the oracle's codes and scales (with its linear equal to quantizer
++ GEMM).
 """
 from __future__ import annotations
 
@@ -115,3 +120,77 @@ def test_fuzz_nvfp4_gemm(M, N, K, oracle):
     ref = oracle.np_nvfp4_gemm(xq.cpu().numpy(), xs.cpu().numpy(), wq.cpu().numpy(),
                                ws.cpu().numpy()) + f32(b)[None, :]
     assert max_rel(out.cpu(), torch.from_numpy(ref)) <= OUT_TOL
+
+
+def _draw_rows(seed: int, count: int, m_max: int, k_mult: int, k_max: int, n_max: int):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(count):
+        M = int(np.exp(rng.uniform(0, np.log(m_max))))
+        K = k_mult * int(rng.integers(1, k_max // k_mult + 1))
+        N = 8 * int(rng.integers(1, n_max // 8 + 1))
+        out.append((M, N, K))
+    return out
+
+
+HOST_SHAPES = _draw_rows(seed=3, count=10, m_max=5000, k_mult=16, k_max=4096, n_max=2048)
+NOALLOC_SHAPES = _draw_rows(seed=5, count=8, m_max=4000, k_mult=16, k_max=4096, n_max=2048)
+MOD_SHAPES = _draw_rows(seed=13, count=12, m_max=2000, k_mult=16, k_max=8192, n_max=1024)
+
+
+@pytest.mark.parametrize("M,N,K", HOST_SHAPES)
+def test_fuzz_host_entry_point(M, N, K, capi):
+    """fp8lin_fp8_linear_host (row chunks of 512 whose upload, kernels and download
+    overlap) gives the device path's bits; x in bf16 or fp16."""
+    from fp8linear_b200 import ops
+
+    dtype = torch.float16 if (M + N) % 2 else torch.bfloat16
+    x, w, b = _x_w_b(M, N, K, seed=M + 3 * N + K)
+    x, w, b = x.to(dtype), w.to(dtype), b.to(dtype)
+    wq, ws = ops.quantize_weight(w)
+    want = capi.fp8_linear(x, wq, ws, b)
+    got = capi.fp8_linear_host(x.cpu().pin_memory(), wq, ws, b)
+    torch.cuda.current_stream().synchronize()
+    assert got.dtype == dtype and torch.equal(got, want.cpu())
+
+
+@pytest.mark.parametrize("M,N,K", NOALLOC_SHAPES)
+def test_fuzz_noalloc_entry_point(M, N, K, capi):
+    """fp8lin_fp8_linear_noalloc (the library's fixed scratch array) gives the bits of
+    fp8lin_fp8_linear (a caller workspace), shape after shape on one scratch."""
+    from fp8linear_b200 import ops
+
+    x, w, b = _x_w_b(M, N, K, seed=M + N + 5 * K)
+    wq, ws = ops.quantize_weight(w)
+    got = capi.fp8_linear_noalloc(x, wq, ws, b)
+    want = capi.fp8_linear(x, wq, ws, b)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("M,N,K", MOD_SHAPES)
+def test_fuzz_modulated(M, N, K, oracle, capi):
+    """LayerNorm + modulation + quantizer bit for bit against the oracle (codes and
+    scales), for 1 to 4 batches of rows, bf16 or fp16; the fused linear (out in x's
+    dtype) equal to quantizer + GEMM with that output type."""
+    import fp8linear_b200 as f
+    from tests.helpers import bits16, codes
+
+    B = 1 + (M + K) % 4
+    M = max(B, M - M % B)  # whole batches of rows
+    dtype = torch.float16 if K % 32 else torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(M * 3 + K)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 1.5 + 0.2).to(dtype)
+    shift = (torch.randn(B, K, device="cuda", generator=g) * 0.1).to(dtype)
+    scale = (torch.randn(B, K, device="cuda", generator=g) * 0.2).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(dtype)
+    wq, ws = f.quantize_weight(w)
+    xq, xs = f.layernorm_modulate_quantize_fp8(x, shift, scale)
+    out = f.fp8_linear_modulated(x, shift, scale, wq, ws, None)
+    two = capi.fp8_gemm(xq, xs, wq, ws, None, out_dtype=dtype)
+    torch.cuda.synchronize()
+    assert out.dtype == dtype and torch.equal(out, two)
+    dt = oracle.BF16 if dtype == torch.bfloat16 else oracle.F16
+    _, oq, osc = oracle.c_ln_modulate_quantize(bits16(x), bits16(shift), bits16(scale), 1e-6, dt)
+    assert np.array_equal(xs.cpu().numpy(), osc)
+    assert np.array_equal(codes(xq), oq)
