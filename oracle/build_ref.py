@@ -2,7 +2,7 @@
 
 Test infrastructure only. The product never imports, links or runs anything
 built here; only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
-reference leg may load it, and only as a checker.
+reference leg may load it, and only as the thing compared against.
 
 The reference sources are compiled where they lie (``<ref>/csrc`` and
 ``<ref>/torch-ext`` of a drbh/fp8linear checkout); nothing is copied into this
@@ -21,7 +21,7 @@ The result is ``oracle/_ref/fp8linear_ref.so``; loading it with
 ``torch.ops.load_library`` registers the reference ops under ``torch.ops.fp8linear_ref``.
 
 Usage: ``python oracle/build_ref.py`` (a no-op when the .so is newer than its sources
-or when the reference tree is absent, e.g. on a GPU box).
+or when the reference tree is absent, e.g. on a machine that only runs prebuilt files).
 """
 from __future__ import annotations
 

@@ -1,7 +1,7 @@
 /*
  * fp8_oracle.c -- CPU restatement of drbh/fp8linear's per-channel FP8 linear path.
  *
- * TEST INFRASTRUCTURE ONLY. This file is the checker that the CUDA kernels of
+ * TEST INFRASTRUCTURE ONLY. This file is the oracle that the CUDA kernels of
  * fp8linear_b200 are compared against; it is never linked into, called by or
  * shipped with the product. Only tests/, __graft_entry__.smoke() and bench.py's
  * CPU-baseline leg load it (through oracle/oracle.py).

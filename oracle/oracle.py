@@ -1,6 +1,6 @@
 """CPU oracle for the per-channel FP8 linear path of drbh/fp8linear.
 
-TEST INFRASTRUCTURE ONLY: the checker for fp8linear_b200's CUDA kernels. Only
+TEST INFRASTRUCTURE ONLY: the oracle for fp8linear_b200's CUDA kernels. Only
 ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
 import it. The product package never imports anything under ``oracle/``.
 
